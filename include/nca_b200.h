@@ -1,0 +1,192 @@
+/*
+ * nca_b200.h -- C ABI of the B200 (sm_100a) Neural Cellular Automaton rollout library.
+ *
+ * The library replaces the test-time rollout hot path of JorisViaudQuantAI/NCAs (a Python /
+ * PyTorch project).  Every entry point below names the reference function or method whose
+ * work it performs; paths are relative to the reference repository root.
+ *
+ * Conventions
+ *  - All pointers marked "device" point to CUDA device memory of the current device.
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).  All work is
+ *    enqueued on that stream; no call synchronises unless it says so.
+ *  - Return values are NcaStatus codes.  Kernel-side failures (a bounded wait that ran out, a
+ *    bounds check) are written to the caller's control words (`ctrl`, 4 x int32, device) and
+ *    reported by nca_b200_ctrl_status().
+ *  - No entry point allocates device memory: the caller provides every buffer, sized by the
+ *    *_bytes() queries.
+ *
+ * State layout.  The reference keeps the state as fp32 NCHW (B, C, H, W).  Inside the library
+ * a state lives in an NcaState workspace: cells are numbered g = inst * H * W + (i * W + j),
+ * grouped into tiles of 128 cells, and stored as [tile][channel/4][128][4] fp32 ("master") plus
+ * an optional bf16 copy [tile][channel/8][128][8] ("mirror") that feeds the perception stencil
+ * in NCA_PREC_BF16 mode.  Both exist twice (ping-pong between steps).
+ */
+#ifndef NCA_B200_H
+#define NCA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NCA_B200_ABI_VERSION 1
+#define NCA_B200_MAX_OUT 16   /* maximum number of readout tokens (n_out) and readout channels */
+
+typedef enum NcaStatus {
+  NCA_OK = 0,
+  NCA_ERR_INVALID = 1,      /* bad argument (null pointer, size mismatch) */
+  NCA_ERR_UNSUPPORTED = 2,  /* a configuration the kernels do not implement */
+  NCA_ERR_CUDA = 3,         /* a CUDA runtime call failed */
+  NCA_ERR_TIMEOUT = 4,      /* a bounded wait inside a kernel ran out (see ctrl words) */
+  NCA_ERR_DEVICE = 5,       /* no sm_100 device, or the kernel image does not load */
+  NCA_ERR_KERNEL = 6        /* a kernel reported an internal check failure (see ctrl words) */
+} NcaStatus;
+
+typedef enum NcaPrecision {
+  NCA_PREC_BF16 = 0,   /* bf16 tcgen05 GEMMs, bf16 stencil source (throughput mode) */
+  NCA_PREC_SPLIT = 1   /* GEMM operands split into bf16 hi + lo parts, fp32 stencil (parity) */
+} NcaPrecision;
+
+typedef enum NcaFireMode {
+  NCA_FIRE_MASK = 0,              /* external {0,1} masks [n_steps][n_inst][H*W] uint8 */
+  NCA_FIRE_PHILOX = 1,            /* u < p_fire, u from in-kernel Philox4x32-10 */
+  NCA_FIRE_ADAPTIVE_PHILOX = 2,   /* u < scale * (1 - conf) + bias, u from Philox */
+  NCA_FIRE_ADAPTIVE_UNIFORM = 3   /* same rule, u from external uniforms [n_steps][n_inst][H*W] */
+} NcaFireMode;
+
+/* The cell rule: KernelPerception (4 heads of 3x3 taps, zero padding) + MLPUpdate + mlp head.
+ * Mirrors nca.model.NCAConfig / NCA (src/nca/model.py:48-137, 161-178, 277-287, 344-345). */
+typedef struct NcaModelDesc {
+  int32_t channels;     /* C: 32 or 64 */
+  int32_t perception;   /* P = 4 * C (heads = 4) */
+  int32_t hidden;       /* Hd: multiple of 32, <= 256 */
+  int32_t c_in, in_offset;    /* clamped input slice [in_offset, in_offset + c_in) */
+  int32_t c_out, out_offset;  /* readout slice [out_offset, out_offset + c_out) */
+  int32_t n_out;              /* number of readout tokens */
+  int32_t fixed_taps;         /* 1: taps are identity, Sobel-x, Sobel-y, Laplacian (fast path) */
+  float taps[4][9];           /* perceive.weight (heads, 1, 3, 3), row-major taps */
+  float head_w[NCA_B200_MAX_OUT][NCA_B200_MAX_OUT]; /* head.weight[o][c] (n_out x c_out) */
+  float head_b[NCA_B200_MAX_OUT];
+  int32_t out_tokens[NCA_B200_MAX_OUT];             /* nca.model.NCAConfig.output_tokens */
+  const void* weights;  /* device: image written by nca_b200_pack_weights + uploaded */
+  const float* b1;      /* device [hidden]   update.fc1.bias */
+  const float* b2;      /* device [channels] update.fc2.bias */
+} NcaModelDesc;
+
+/* A batch of instances (board x trial rows of the reference's flattened batch,
+ * src/nca/rollout.py:144-150).  Instance `inst` uses clamp row inst_row[inst], or inst / trials
+ * when inst_row is NULL. */
+typedef struct NcaBatchDesc {
+  int32_t n_inst, height, width;
+  int32_t trials;           /* K */
+  int64_t inst_offset;      /* global index of instance 0 (Philox counters; shards agree) */
+  const uint8_t* given;     /* device [rows][H*W] 1 = clamped cell (given4) */
+  const float* clamp;       /* device [rows][H*W][c_in] clamp values (embedding of the input) */
+  const uint8_t* inputs;    /* device [rows][H*W] input tokens (readout fills given cells) */
+  const int32_t* inst_row;  /* optional device [n_inst] */
+} NcaBatchDesc;
+
+typedef struct NcaState {
+  int32_t n_inst, hw, channels, precision;
+  int64_t n_tiles;          /* ceil(n_inst * hw / 128) */
+  float* master[2];         /* device, tiled fp32 */
+  uint16_t* mirror[2];      /* device, tiled bf16 (NULL in NCA_PREC_SPLIT) */
+  int32_t cur;              /* index of the buffers holding the current state */
+} NcaState;
+
+typedef struct NcaFireDesc {
+  int32_t mode;             /* NcaFireMode */
+  float p_fire;             /* RolloutConfig.fire_rate */
+  float adapt_scale, adapt_bias;  /* p = scale * (1 - conf_cell) + bias */
+  uint64_t seed;            /* Philox key */
+  int64_t step0;            /* absolute index of the first step of this call */
+  const uint8_t* masks;     /* device [n_steps][n_inst][H*W] (NCA_FIRE_MASK) */
+  const float* uniforms;    /* device [n_steps][n_inst][H*W] (NCA_FIRE_ADAPTIVE_UNIFORM) */
+  uint32_t* updates;        /* optional device [n_inst]: fired cells are added here */
+} NcaFireDesc;
+
+/* ---- library / device --------------------------------------------------------------------- */
+int32_t nca_b200_abi_version(void);
+const char* nca_b200_status_string(int32_t status);
+/* Checks that `device` is an sm_100 part and that the kernels load on it. */
+int32_t nca_b200_device_info(int32_t device, int32_t* sm_count, int32_t* cc_major,
+                             int32_t* cc_minor);
+
+/* ---- weights ------------------------------------------------------------------------------ */
+/* Host-side: bytes of the packed bf16 weight image (fc1 then fc2, 128B-swizzled K-major). */
+int32_t nca_b200_weights_bytes(int32_t channels, int32_t perception, int32_t hidden,
+                               size_t* bytes);
+/* Host-side packing of update.fc1.weight (hidden x perception) and update.fc2.weight
+ * (channels x hidden), fp32 row-major, into the image.  Replaces the fp32->bf16 weight cast the
+ * reference's Triton MLP does per call (src/nca/engine/triton_mlp.py:138-156). */
+int32_t nca_b200_pack_weights(const float* w1, const float* w2, int32_t channels,
+                              int32_t perception, int32_t hidden, void* image_host);
+
+/* ---- state -------------------------------------------------------------------------------- */
+int32_t nca_b200_state_bytes(int32_t n_inst, int32_t hw, int32_t channels, int32_t precision,
+                             size_t* bytes);
+/* Carves an NcaState out of a caller buffer of nca_b200_state_bytes() bytes (256-B aligned). */
+int32_t nca_b200_state_bind(NcaState* st, void* buffer, size_t bytes, int32_t n_inst,
+                            int32_t hw, int32_t channels, int32_t precision);
+/* Zero state + clamp of the given cells: nca.model.NCA.init_state with sigma_init = 0
+ * (src/nca/model.py:384-412, apply_clamp 430-438). */
+int32_t nca_b200_state_init(NcaState* st, const NcaModelDesc* m, const NcaBatchDesc* b,
+                            void* stream);
+/* fp32 NCHW (n_inst, C, H, W) <-> NcaState.  The reference's state format
+ * (src/nca/model.py:29-30). */
+int32_t nca_b200_state_load_nchw(NcaState* st, const float* x_nchw, void* stream);
+int32_t nca_b200_state_store_nchw(const NcaState* st, float* x_nchw, void* stream);
+
+/* ---- the rollout step --------------------------------------------------------------------- */
+/* n_steps NCA steps on every instance: perception stencil, MLP on tcgen05, fire mask, residual
+ * update, clamp.  Replaces nca.model.NCA.step (src/nca/model.py:503-525, residual_update
+ * 527-559, sample_fire_mask 567-593) looped by nca.rollout.rollout (src/nca/rollout.py:203-247)
+ * and nca.engine.inference.UniformRolloutBlocks.__call__ (src/nca/engine/inference.py:98-104).
+ * n_steps > 1 runs as one persistent cooperative launch with a bounded grid barrier per step.
+ * `ctrl` is 4 x int32 device control words (error code, detail, barrier, abort). */
+int32_t nca_b200_run_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaState* st,
+                           int32_t n_steps, const NcaFireDesc* fire, int32_t* ctrl,
+                           int32_t timeout_ms, void* stream);
+
+/* ---- readout, selection, pruning ---------------------------------------------------------- */
+/* Per cell: argmax token of the mlp head (given cells show their input token) and max-softmax
+ * confidence; per instance: mean confidence over all H*W cells and, with `targets`, the
+ * fraction of mutable cells correct and the exact flag.  Replaces NCA.decode / confidence /
+ * board_confidence (src/nca/model.py:596-633), decode_boards (src/nca/rollout.py:74-82) and the
+ * rollout's score() (src/nca/rollout.py:181-184).  Any output pointer may be NULL. */
+int32_t nca_b200_readout(const NcaModelDesc* m, const NcaBatchDesc* b, const NcaState* st,
+                         uint8_t* pred, float* cell_conf, float* board_conf,
+                         const uint8_t* targets, float* cell_acc, uint8_t* exact,
+                         void* stream);
+/* conf@K selection: per board the first index of the largest confidence among alive trials
+ * k < k_limit (np.argmax semantics), its confidence and (optionally) its decoded grid.
+ * Replaces the selection inside nca.rollout.conf_at_k (src/nca/rollout.py:317-334). */
+int32_t nca_b200_select(const float* board_conf, const uint8_t* alive, int32_t n_boards,
+                        int32_t trials, int32_t k_limit, int32_t* best_idx, float* best_conf,
+                        const uint8_t* pred, int32_t hw, uint8_t* best_pred, void* stream);
+/* Niche-capped pruning with refill: trials whose decoded grids are byte-identical form a niche
+ * (grouping of src/nca/pruning.py:39-41); each niche keeps its n_cap most confident members
+ * (stable sort, src/nca/pruning.py:43-46); every dropped slot is refilled with a clone of a
+ * kept trial, kept trials taken in decreasing confidence, cycling.  Writes src[inst] (the
+ * instance whose state slot `inst` continues from) and kept[inst]. */
+int32_t nca_b200_prune_refill(const uint8_t* pred, const float* board_conf, int32_t n_boards,
+                              int32_t trials, int32_t hw, int32_t n_cap, int32_t* src,
+                              uint8_t* kept, void* stream);
+/* Copies the state of instance src[i] into instance i wherever src[i] != i (the batch gather
+ * x[sel] of src/nca/rollout.py:270-274, without compaction). */
+int32_t nca_b200_clone(NcaState* st, const int32_t* src, void* stream);
+
+/* ---- control words ------------------------------------------------------------------------ */
+/* Synchronises `stream`, reads the control words and returns NCA_OK or the first kernel-side
+ * error; detail (may be NULL) receives the failing site.  Clears the words on return. */
+int32_t nca_b200_ctrl_status(int32_t* ctrl, int32_t* detail, void* stream);
+/* Self-test of the bounded waits: launches a kernel that waits for a flag nothing sets, with
+ * the given timeout; returns NCA_ERR_TIMEOUT (the expected result) when the wait gave up. */
+int32_t nca_b200_selftest_timeout(int32_t* ctrl, int32_t timeout_ms, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NCA_B200_H */

@@ -1,0 +1,658 @@
+// api.cu -- C ABI of libnca_b200 (declared in include/nca_b200.h): host entry points, the step
+// kernel instantiations and the small kernels around it (state layout conversion, readout,
+// conf@K selection, niche-capped pruning with refill, state cloning).
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "../../include/nca_b200.h"
+#include "step_kernel.cuh"
+
+using namespace nca;
+
+namespace {
+
+constexpr int kMaxSmem = 232448;  // opt-in dynamic shared memory per CTA on sm_100
+
+inline int32_t cuda_status(cudaError_t e) { return e == cudaSuccess ? NCA_OK : NCA_ERR_CUDA; }
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline long long n_tiles_of(long long cells) { return (cells + kTileM - 1) / kTileM; }
+
+inline size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// ------------------------------------------------------------------------------ bf16 (host)
+inline uint16_t f32_to_bf16_rne(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x7FFFFFu)) return (uint16_t)((u >> 16) | 0x40);
+  const uint32_t lsb = (u >> 16) & 1u;
+  u += 0x7FFFu + lsb;
+  return (uint16_t)(u >> 16);
+}
+
+// Writes a (rows x K) row-major fp32 matrix as the K-major, 128B-swizzled bf16 image that a
+// tcgen05 shared-memory descriptor with SWIZZLE_128B reads: K in blocks of 64, each block
+// [rows][128 B], 16-byte chunk c of row r stored at chunk position c ^ (r & 7).
+void pack_sw128(const float* w, int rows, int K, uint16_t* out) {
+  const int kb_n = K / 64;
+  for (int kb = 0; kb < kb_n; ++kb)
+    for (int r = 0; r < rows; ++r)
+      for (int c = 0; c < 8; ++c)
+        for (int e = 0; e < 8; ++e) {
+          const int k = kb * 64 + c * 8 + e;
+          const size_t dst = (size_t)kb * rows * 64 + (size_t)r * 64 + ((c ^ (r & 7)) * 8) + e;
+          out[dst] = f32_to_bf16_rne(w[(size_t)r * K + k]);
+        }
+}
+
+// ------------------------------------------------------------------------- state kernels
+__device__ __forceinline__ float clamp_value(const NcaBatchDesc& b, int c_in, int in_off, int inst,
+                                             int p, int c, float v) {
+  const int row = b.inst_row ? b.inst_row[inst] : inst / b.trials;
+  const int ci = c - in_off;
+  if (ci >= 0 && ci < c_in && b.given[(long long)row * b.height * b.width + p])
+    return b.clamp[((long long)row * b.height * b.width + p) * c_in + ci];
+  return v;
+}
+
+// One thread per (tile, 8-channel group, row): writes 8 channels of one cell.
+// mode 0: zero state + clamp; mode 1: load from NCHW.
+__global__ void state_fill_kernel(float* master, uint16_t* mirror, int C, long long n_tiles,
+                                  long long total, int hw, NcaBatchDesc b, int c_in, int in_off,
+                                  const float* x_nchw, int mode) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int C8 = C / 8;
+  if (idx >= n_tiles * C8 * kTileM) return;
+  const int m = (int)(idx & 127);
+  const long long rest = idx >> 7;
+  const int c8 = (int)(rest % C8);
+  const long long t = rest / C8;
+  const long long g = t * kTileM + m;
+  float v[8];
+  for (int e = 0; e < 8; ++e) v[e] = 0.f;
+  if (g < total) {
+    const int inst = (int)(g / hw);
+    const int p = (int)(g - (long long)inst * hw);
+    for (int e = 0; e < 8; ++e) {
+      const int c = c8 * 8 + e;
+      float x = 0.f;
+      if (mode == 1) x = x_nchw[((long long)inst * C + c) * hw + p];
+      else x = clamp_value(b, c_in, in_off, inst, p, c, 0.f);
+      v[e] = x;
+    }
+  }
+  for (int hq = 0; hq < 2; ++hq) {
+    const int c4 = c8 * 2 + hq;
+    *reinterpret_cast<float4*>(master + ((t * (C / 4) + c4) * kTileM + m) * 4) =
+        make_float4(v[hq * 4 + 0], v[hq * 4 + 1], v[hq * 4 + 2], v[hq * 4 + 3]);
+  }
+  if (mirror) {
+    uint4 pk;
+    pk.x = pack_bf16(v[0], v[1]);
+    pk.y = pack_bf16(v[2], v[3]);
+    pk.z = pack_bf16(v[4], v[5]);
+    pk.w = pack_bf16(v[6], v[7]);
+    *reinterpret_cast<uint4*>(mirror + ((t * (C / 8) + c8) * kTileM + m) * 8) = pk;
+  }
+}
+
+__global__ void state_store_kernel(const float* master, int C, long long total, int hw,
+                                   float* x_nchw) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= total * C) return;
+  // idx enumerates NCHW order: ((inst * C + c) * hw + p)
+  const int p = (int)(idx % hw);
+  const long long r = idx / hw;
+  const int c = (int)(r % C);
+  const long long inst = r / C;
+  const long long g = inst * hw + p;
+  const long long t = g >> 7;
+  const int m = (int)(g & 127);
+  x_nchw[idx] = master[((t * (C / 4) + (c >> 2)) * kTileM + m) * 4 + (c & 3)];
+}
+
+// ------------------------------------------------------------------------------- readout
+struct ReadoutArgs {
+  int C, hw, n_inst, c_out, out_off, n_out;
+  float head_w[16][16];
+  float head_b[16];
+  int out_tokens[16];
+};
+
+// One block per instance.  Scores of the mlp head on the readout slice, argmax (first maximum,
+// as torch.argmax), max-softmax confidence clamped to [0, 1] (src/nca/model.py:596-633).
+__global__ void readout_kernel(const float* master, NcaBatchDesc b, ReadoutArgs R, uint8_t* pred,
+                               float* cell_conf, float* board_conf, const uint8_t* targets,
+                               float* cell_acc, uint8_t* exact) {
+  const int inst = blockIdx.x;
+  const int row = b.inst_row ? b.inst_row[inst] : inst / b.trials;
+  float conf_sum = 0.f, correct = 0.f, n_mut = 0.f;
+  for (int p = threadIdx.x; p < R.hw; p += blockDim.x) {
+    const long long g = (long long)inst * R.hw + p;
+    const long long t = g >> 7;
+    const int m = (int)(g & 127);
+    float xo[16];
+    for (int c = 0; c < R.c_out; ++c) {
+      const int cc = R.out_off + c;
+      xo[c] = master[((t * (R.C / 4) + (cc >> 2)) * kTileM + m) * 4 + (cc & 3)];
+    }
+    float best = -3.402823466e38f;
+    int arg = 0;
+    float sc[16];
+    for (int o = 0; o < R.n_out; ++o) {
+      float a = R.head_b[o];
+      for (int c = 0; c < R.c_out; ++c) a = fmaf(R.head_w[o][c], xo[c], a);
+      sc[o] = a;
+      if (a > best || o == 0) { best = a; arg = o; }
+    }
+    float den = 0.f;
+    for (int o = 0; o < R.n_out; ++o) den += expf(sc[o] - best);
+    const float conf = fminf(fmaxf(1.f / den, 0.f), 1.f);
+    conf_sum += conf;
+    const long long bp = (long long)row * R.hw + p;
+    const bool gv = b.given[bp] != 0;
+    const int tok = gv ? (int)b.inputs[bp] : R.out_tokens[arg];
+    if (pred) pred[(long long)inst * R.hw + p] = (uint8_t)tok;
+    if (cell_conf) cell_conf[(long long)inst * R.hw + p] = conf;
+    if (targets && !gv) {
+      n_mut += 1.f;
+      correct += (tok == (int)targets[bp]) ? 1.f : 0.f;
+    }
+  }
+  __shared__ float red[3][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int o = 16; o; o >>= 1) {
+    conf_sum += __shfl_xor_sync(0xffffffffu, conf_sum, o);
+    correct += __shfl_xor_sync(0xffffffffu, correct, o);
+    n_mut += __shfl_xor_sync(0xffffffffu, n_mut, o);
+  }
+  if (lane == 0) { red[0][w] = conf_sum; red[1][w] = correct; red[2][w] = n_mut; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float a = 0.f, c = 0.f, n = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) { a += red[0][i]; c += red[1][i]; n += red[2][i]; }
+    if (board_conf) board_conf[inst] = a / (float)R.hw;
+    if (targets) {
+      const float nm = fmaxf(n, 1.f);
+      if (cell_acc) cell_acc[inst] = c / nm;
+      if (exact) exact[inst] = (c == nm) ? 1 : 0;
+    }
+  }
+}
+
+// One warp per board: first index of the maximum of (alive ? conf : -inf) over k < k_limit.
+__global__ void select_kernel(const float* conf, const uint8_t* alive, int n_boards, int K,
+                              int k_limit, int* best_idx, float* best_conf, const uint8_t* pred,
+                              int hw, uint8_t* best_pred) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= n_boards) return;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int k = lane; k < k_limit; k += 32) {
+    const long long i = (long long)warp * K + k;
+    const float v = (alive == nullptr || alive[i]) ? conf[i] : -INFINITY;
+    if (v > bv || (v == bv && k < bi)) { bv = v; bi = k; }
+  }
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  if (bi == 0x7fffffff) bi = 0;
+  if (lane == 0) {
+    if (best_idx) best_idx[warp] = bi;
+    if (best_conf) best_conf[warp] = bv;
+  }
+  if (pred && best_pred) {
+    const uint8_t* src = pred + ((long long)warp * K + bi) * hw;
+    for (int p = lane; p < hw; p += 32) best_pred[(long long)warp * hw + p] = src[p];
+  }
+}
+
+// FNV-1a 64-bit over the decoded grid (Fowler, Noll, Vo; public-domain hash).
+__device__ __forceinline__ uint64_t fnv1a64(const uint8_t* p, int n) {
+  uint64_t h = 1469598103934665603ull;
+  for (int i = 0; i < n; ++i) { h ^= p[i]; h *= 1099511628211ull; }
+  return h;
+}
+
+// One block of K threads per board.
+__global__ void prune_refill_kernel(const uint8_t* pred, const float* conf, int K, int hw,
+                                    int n_cap, int* src, uint8_t* kept_out) {
+  extern __shared__ uint8_t sm[];
+  uint64_t* hsh = reinterpret_cast<uint64_t*>(sm);
+  float* cf = reinterpret_cast<float*>(hsh + K);
+  int* niche = reinterpret_cast<int*>(cf + K);
+  int* kept = niche + K;
+  int* by_rank = kept + K;
+  const int board = blockIdx.x;
+  const int k = threadIdx.x;
+  const uint8_t* base = pred + (long long)board * K * hw;
+  if (k < K) {
+    hsh[k] = fnv1a64(base + (long long)k * hw, hw);
+    cf[k] = conf[(long long)board * K + k];
+  }
+  __syncthreads();
+  if (k < K) {
+    int nid = k;
+    for (int j = 0; j < k; ++j) {
+      if (hsh[j] != hsh[k]) continue;
+      const uint8_t* a = base + (long long)j * hw;
+      const uint8_t* b = base + (long long)k * hw;
+      bool eq = true;
+      for (int p = 0; p < hw; ++p)
+        if (a[p] != b[p]) { eq = false; break; }
+      if (eq) { nid = j; break; }
+    }
+    niche[k] = nid;
+  }
+  __syncthreads();
+  if (k < K) {
+    int rank = 0;
+    for (int j = 0; j < K; ++j)
+      if (niche[j] == niche[k] && (cf[j] > cf[k] || (cf[j] == cf[k] && j < k))) ++rank;
+    kept[k] = rank < n_cap ? 1 : 0;
+  }
+  __syncthreads();
+  int n_kept = 0;
+  for (int j = 0; j < K; ++j) n_kept += kept[j];
+  if (k < K && kept[k]) {
+    int srank = 0;
+    for (int j = 0; j < K; ++j)
+      if (kept[j] && (cf[j] > cf[k] || (cf[j] == cf[k] && j < k))) ++srank;
+    by_rank[srank] = k;
+  }
+  __syncthreads();
+  if (k < K) {
+    int s = k;
+    if (!kept[k]) {
+      int d = 0;
+      for (int j = 0; j < k; ++j) d += kept[j] ? 0 : 1;
+      s = by_rank[d % n_kept];
+    }
+    src[(long long)board * K + k] = board * K + s;
+    if (kept_out) kept_out[(long long)board * K + k] = (uint8_t)kept[k];
+  }
+}
+
+// One thread per (instance, cell, 4-channel chunk) of the destination.
+__global__ void clone_kernel(float* master, uint16_t* mirror, int C, int hw, int n_inst,
+                             const int* src) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int C4 = C / 4;
+  if (idx >= (long long)n_inst * hw * C4) return;
+  const int c4 = (int)(idx % C4);
+  const long long cell = idx / C4;
+  const int inst = (int)(cell / hw);
+  const int p = (int)(cell - (long long)inst * hw);
+  const int s = src[inst];
+  if (s == inst) return;
+  const long long gd = (long long)inst * hw + p, gs = (long long)s * hw + p;
+  const long long od = (((gd >> 7) * C4 + c4) << 7) + (gd & 127);
+  const long long os = (((gs >> 7) * C4 + c4) << 7) + (gs & 127);
+  reinterpret_cast<float4*>(master)[od] = reinterpret_cast<const float4*>(master)[os];
+  if (mirror && (c4 & 1) == 0) {
+    const int C8 = C / 8, c8 = c4 >> 1;
+    const long long md = (((gd >> 7) * C8 + c8) << 7) + (gd & 127);
+    const long long ms = (((gs >> 7) * C8 + c8) << 7) + (gs & 127);
+    reinterpret_cast<uint4*>(mirror)[md] = reinterpret_cast<const uint4*>(mirror)[ms];
+  }
+}
+
+__global__ void selftest_wait_kernel(int* ctrl, unsigned long long timeout_ns) {
+  __shared__ int abort_flag;
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  FailState fs;
+  fs.ctrl = ctrl;
+  fs.cta_abort = &abort_flag;
+  fs.timeout_ns = timeout_ns;
+  fs.deadline_ns = 0;
+  // Nothing ever arrives on `bar`: the bounded wait must give up and report a timeout.
+  if (threadIdx.x < 32) warp_wait(&bar, 0, fs, 99);
+  __syncthreads();
+}
+
+template <class Cfg>
+int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaState* st, int32_t n_steps,
+                     const NcaFireDesc* fire, int32_t* ctrl, int32_t timeout_ms,
+                     cudaStream_t stream) {
+  StepArgs A;
+  memset(&A, 0, sizeof(A));
+  A.n_inst = b->n_inst;
+  A.H = b->height;
+  A.W = b->width;
+  A.HW = b->height * b->width;
+  A.K = b->trials;
+  A.total = (long long)b->n_inst * A.HW;
+  A.n_tiles = st->n_tiles;
+  A.inst_offset = b->inst_offset;
+  A.n_steps = n_steps;
+  A.step0 = fire->step0;
+  A.win_cells = kTileM + 2 * b->width + 2;
+  A.c_in = m->c_in;
+  A.in_off = m->in_offset;
+  A.c_out = m->c_out;
+  A.out_off = m->out_offset;
+  A.n_out = m->n_out;
+  A.fixed_taps = m->fixed_taps;
+  memcpy(A.taps, m->taps, sizeof(A.taps));
+  memcpy(A.head_w, m->head_w, sizeof(A.head_w));
+  memcpy(A.head_b, m->head_b, sizeof(A.head_b));
+  A.wimg = reinterpret_cast<const uint8_t*>(m->weights);
+  A.b1 = m->b1;
+  A.b2 = m->b2;
+  A.given = b->given;
+  A.clamp = b->clamp;
+  A.inst_row = b->inst_row;
+  A.master[0] = st->master[0];
+  A.master[1] = st->master[1];
+  A.mirror[0] = st->mirror[0];
+  A.mirror[1] = st->mirror[1];
+  A.cur = st->cur;
+  A.fire_mode = fire->mode;
+  A.p_fire = fire->p_fire;
+  A.ad_scale = fire->adapt_scale;
+  A.ad_bias = fire->adapt_bias;
+  A.seed = fire->seed;
+  A.masks = fire->masks;
+  A.uniforms = fire->uniforms;
+  A.updates = fire->updates;
+  A.ctrl = ctrl;
+  A.timeout_ns = (unsigned long long)(timeout_ms > 0 ? timeout_ms : 10000) * 1000000ull;
+
+  int stages = 2;
+  int smem = SmemLayout<Cfg>(stages, A.win_cells).total + 1024;
+  if (smem > kMaxSmem) {
+    stages = 1;
+    smem = SmemLayout<Cfg>(stages, A.win_cells).total + 1024;
+  }
+  if (smem > kMaxSmem) return NCA_ERR_UNSUPPORTED;
+  A.stages = stages;
+
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return NCA_ERR_CUDA;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return NCA_ERR_CUDA;
+  auto kern = nca_step_kernel<Cfg>;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return NCA_ERR_CUDA;
+  const long long grid_ll = A.n_tiles < sms ? A.n_tiles : sms;
+  const int grid = (int)(grid_ll > 0 ? grid_ll : 1);
+  e = cudaMemsetAsync(ctrl + 2, 0, sizeof(int32_t), stream);
+  if (e != cudaSuccess) return NCA_ERR_CUDA;
+  if (n_steps > 1) {
+    void* args[] = {&A};
+    e = cudaLaunchCooperativeKernel((const void*)kern, dim3(grid), dim3(kThreads), args,
+                                    (size_t)smem, stream);
+  } else {
+    kern<<<grid, kThreads, smem, stream>>>(A);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) return NCA_ERR_CUDA;
+  st->cur = (st->cur + n_steps) & 1;
+  return NCA_OK;
+}
+
+bool model_ok(const NcaModelDesc* m) {
+  if (!m || !m->weights || !m->b1 || !m->b2) return false;
+  if (m->perception != 4 * m->channels) return false;
+  if (m->c_in < 0 || m->in_offset < 0 || m->in_offset + m->c_in > m->channels) return false;
+  if (m->c_out < 1 || m->c_out > NCA_B200_MAX_OUT || m->out_offset < 0 ||
+      m->out_offset + m->c_out > m->channels)
+    return false;
+  if (m->n_out < 1 || m->n_out > NCA_B200_MAX_OUT) return false;
+  return true;
+}
+
+bool batch_ok(const NcaBatchDesc* b) {
+  return b && b->n_inst > 0 && b->height > 0 && b->width > 0 && b->trials > 0 && b->given &&
+         b->clamp;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t nca_b200_abi_version(void) { return NCA_B200_ABI_VERSION; }
+
+const char* nca_b200_status_string(int32_t s) {
+  switch (s) {
+    case NCA_OK: return "ok";
+    case NCA_ERR_INVALID: return "invalid argument";
+    case NCA_ERR_UNSUPPORTED: return "unsupported configuration";
+    case NCA_ERR_CUDA: return "CUDA runtime error";
+    case NCA_ERR_TIMEOUT: return "a bounded wait inside a kernel ran out";
+    case NCA_ERR_DEVICE: return "no usable sm_100 device";
+    case NCA_ERR_KERNEL: return "kernel-side check failed";
+    default: return "unknown status";
+  }
+}
+
+int32_t nca_b200_device_info(int32_t device, int32_t* sm_count, int32_t* cc_major,
+                             int32_t* cc_minor) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return NCA_ERR_DEVICE;
+  int sms = 0, ma = 0, mi = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+      cudaDeviceGetAttribute(&ma, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess ||
+      cudaDeviceGetAttribute(&mi, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess)
+    return NCA_ERR_CUDA;
+  if (sm_count) *sm_count = sms;
+  if (cc_major) *cc_major = ma;
+  if (cc_minor) *cc_minor = mi;
+  if (ma != 10) return NCA_ERR_DEVICE;
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, nca_step_kernel<StepCfg<64, 256, false>>) != cudaSuccess)
+    return NCA_ERR_DEVICE;
+  return NCA_OK;
+}
+
+int32_t nca_b200_weights_bytes(int32_t channels, int32_t perception, int32_t hidden,
+                               size_t* bytes) {
+  if (!bytes || channels <= 0 || perception <= 0 || hidden <= 0) return NCA_ERR_INVALID;
+  if (perception % 64 || hidden % 64 || channels % 8) return NCA_ERR_UNSUPPORTED;
+  *bytes = ((size_t)hidden * perception + (size_t)channels * hidden) * 2;
+  return NCA_OK;
+}
+
+int32_t nca_b200_pack_weights(const float* w1, const float* w2, int32_t channels,
+                              int32_t perception, int32_t hidden, void* image_host) {
+  size_t bytes = 0;
+  int32_t s = nca_b200_weights_bytes(channels, perception, hidden, &bytes);
+  if (s != NCA_OK) return s;
+  if (!w1 || !w2 || !image_host) return NCA_ERR_INVALID;
+  uint16_t* out = reinterpret_cast<uint16_t*>(image_host);
+  pack_sw128(w1, hidden, perception, out);
+  pack_sw128(w2, channels, hidden, out + (size_t)hidden * perception);
+  return NCA_OK;
+}
+
+int32_t nca_b200_state_bytes(int32_t n_inst, int32_t hw, int32_t channels, int32_t precision,
+                             size_t* bytes) {
+  if (!bytes || n_inst <= 0 || hw <= 0 || channels <= 0 || channels % 16) return NCA_ERR_INVALID;
+  const long long tiles = n_tiles_of((long long)n_inst * hw);
+  const size_t master = align256((size_t)tiles * kTileM * channels * 4);
+  const size_t mirror = precision == NCA_PREC_BF16 ? align256((size_t)tiles * kTileM * channels * 2) : 0;
+  *bytes = 2 * master + 2 * mirror;
+  return NCA_OK;
+}
+
+int32_t nca_b200_state_bind(NcaState* st, void* buffer, size_t bytes, int32_t n_inst, int32_t hw,
+                            int32_t channels, int32_t precision) {
+  size_t need = 0;
+  int32_t s = nca_b200_state_bytes(n_inst, hw, channels, precision, &need);
+  if (s != NCA_OK) return s;
+  if (!st || !buffer || bytes < need || (reinterpret_cast<uintptr_t>(buffer) & 255))
+    return NCA_ERR_INVALID;
+  if (precision != NCA_PREC_BF16 && precision != NCA_PREC_SPLIT) return NCA_ERR_INVALID;
+  const long long tiles = n_tiles_of((long long)n_inst * hw);
+  const size_t master = align256((size_t)tiles * kTileM * channels * 4);
+  const size_t mirror = precision == NCA_PREC_BF16 ? align256((size_t)tiles * kTileM * channels * 2) : 0;
+  uint8_t* p = reinterpret_cast<uint8_t*>(buffer);
+  st->n_inst = n_inst;
+  st->hw = hw;
+  st->channels = channels;
+  st->precision = precision;
+  st->n_tiles = tiles;
+  st->master[0] = reinterpret_cast<float*>(p);
+  st->master[1] = reinterpret_cast<float*>(p + master);
+  st->mirror[0] = mirror ? reinterpret_cast<uint16_t*>(p + 2 * master) : nullptr;
+  st->mirror[1] = mirror ? reinterpret_cast<uint16_t*>(p + 2 * master + mirror) : nullptr;
+  st->cur = 0;
+  return NCA_OK;
+}
+
+int32_t nca_b200_state_init(NcaState* st, const NcaModelDesc* m, const NcaBatchDesc* b,
+                            void* stream) {
+  if (!st || !m || !batch_ok(b) || b->n_inst != st->n_inst || b->height * b->width != st->hw)
+    return NCA_ERR_INVALID;
+  const long long n = st->n_tiles * (st->channels / 8) * kTileM;
+  const int bs = 256;
+  state_fill_kernel<<<(unsigned)((n + bs - 1) / bs), bs, 0, as_stream(stream)>>>(
+      st->master[st->cur], st->mirror[st->cur], st->channels, st->n_tiles,
+      (long long)st->n_inst * st->hw, st->hw, *b, m->c_in, m->in_offset, nullptr, 0);
+  return cuda_status(cudaGetLastError());
+}
+
+int32_t nca_b200_state_load_nchw(NcaState* st, const float* x_nchw, void* stream) {
+  if (!st || !x_nchw) return NCA_ERR_INVALID;
+  NcaBatchDesc dummy;
+  memset(&dummy, 0, sizeof(dummy));
+  dummy.trials = 1;
+  const long long n = st->n_tiles * (st->channels / 8) * kTileM;
+  const int bs = 256;
+  state_fill_kernel<<<(unsigned)((n + bs - 1) / bs), bs, 0, as_stream(stream)>>>(
+      st->master[st->cur], st->mirror[st->cur], st->channels, st->n_tiles,
+      (long long)st->n_inst * st->hw, st->hw, dummy, 0, 0, x_nchw, 1);
+  return cuda_status(cudaGetLastError());
+}
+
+int32_t nca_b200_state_store_nchw(const NcaState* st, float* x_nchw, void* stream) {
+  if (!st || !x_nchw) return NCA_ERR_INVALID;
+  const long long n = (long long)st->n_inst * st->hw * st->channels;
+  const int bs = 256;
+  state_store_kernel<<<(unsigned)((n + bs - 1) / bs), bs, 0, as_stream(stream)>>>(
+      st->master[st->cur], st->channels, (long long)st->n_inst * st->hw, st->hw, x_nchw);
+  return cuda_status(cudaGetLastError());
+}
+
+int32_t nca_b200_run_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaState* st,
+                           int32_t n_steps, const NcaFireDesc* fire, int32_t* ctrl,
+                           int32_t timeout_ms, void* stream) {
+  if (!model_ok(m) || !batch_ok(b) || !st || !fire || !ctrl || n_steps < 0) return NCA_ERR_INVALID;
+  if (b->n_inst != st->n_inst || b->height * b->width != st->hw || m->channels != st->channels)
+    return NCA_ERR_INVALID;
+  if (fire->mode == NCA_FIRE_MASK && !fire->masks) return NCA_ERR_INVALID;
+  if (fire->mode == NCA_FIRE_ADAPTIVE_UNIFORM && !fire->uniforms) return NCA_ERR_INVALID;
+  if (fire->mode < 0 || fire->mode > 3) return NCA_ERR_INVALID;
+  if (n_steps == 0) return NCA_OK;
+  const bool split = st->precision == NCA_PREC_SPLIT;
+  cudaStream_t s = as_stream(stream);
+  const int C = m->channels, HD = m->hidden;
+  if (C == 32 && HD == 128) {
+    return split ? launch_steps<StepCfg<32, 128, true>>(m, b, st, n_steps, fire, ctrl, timeout_ms, s)
+                 : launch_steps<StepCfg<32, 128, false>>(m, b, st, n_steps, fire, ctrl, timeout_ms, s);
+  }
+  if (C == 64 && HD == 256) {
+    return split ? launch_steps<StepCfg<64, 256, true>>(m, b, st, n_steps, fire, ctrl, timeout_ms, s)
+                 : launch_steps<StepCfg<64, 256, false>>(m, b, st, n_steps, fire, ctrl, timeout_ms, s);
+  }
+  return NCA_ERR_UNSUPPORTED;
+}
+
+int32_t nca_b200_readout(const NcaModelDesc* m, const NcaBatchDesc* b, const NcaState* st,
+                         uint8_t* pred, float* cell_conf, float* board_conf,
+                         const uint8_t* targets, float* cell_acc, uint8_t* exact, void* stream) {
+  if (!model_ok(m) || !batch_ok(b) || !st || !b->inputs) return NCA_ERR_INVALID;
+  if (b->n_inst != st->n_inst || b->height * b->width != st->hw) return NCA_ERR_INVALID;
+  ReadoutArgs R;
+  memset(&R, 0, sizeof(R));
+  R.C = st->channels;
+  R.hw = st->hw;
+  R.n_inst = st->n_inst;
+  R.c_out = m->c_out;
+  R.out_off = m->out_offset;
+  R.n_out = m->n_out;
+  memcpy(R.head_w, m->head_w, sizeof(R.head_w));
+  memcpy(R.head_b, m->head_b, sizeof(R.head_b));
+  memcpy(R.out_tokens, m->out_tokens, sizeof(R.out_tokens));
+  readout_kernel<<<st->n_inst, 128, 0, as_stream(stream)>>>(st->master[st->cur], *b, R, pred,
+                                                           cell_conf, board_conf, targets,
+                                                           cell_acc, exact);
+  return cuda_status(cudaGetLastError());
+}
+
+int32_t nca_b200_select(const float* board_conf, const uint8_t* alive, int32_t n_boards,
+                        int32_t trials, int32_t k_limit, int32_t* best_idx, float* best_conf,
+                        const uint8_t* pred, int32_t hw, uint8_t* best_pred, void* stream) {
+  if (!board_conf || n_boards <= 0 || trials <= 0 || k_limit <= 0) return NCA_ERR_INVALID;
+  if (k_limit > trials) k_limit = trials;
+  const int threads = 256;
+  const int blocks = (n_boards * 32 + threads - 1) / threads;
+  select_kernel<<<blocks, threads, 0, as_stream(stream)>>>(board_conf, alive, n_boards, trials,
+                                                           k_limit, best_idx, best_conf, pred, hw,
+                                                           best_pred);
+  return cuda_status(cudaGetLastError());
+}
+
+int32_t nca_b200_prune_refill(const uint8_t* pred, const float* board_conf, int32_t n_boards,
+                              int32_t trials, int32_t hw, int32_t n_cap, int32_t* src,
+                              uint8_t* kept, void* stream) {
+  if (!pred || !board_conf || !src || n_boards <= 0 || trials <= 0 || hw <= 0 || n_cap < 1)
+    return NCA_ERR_INVALID;
+  if (trials > 1024) return NCA_ERR_UNSUPPORTED;
+  const size_t sm = (size_t)trials * (8 + 4 + 4 + 4 + 4);
+  const int threads = ((trials + 31) / 32) * 32;
+  prune_refill_kernel<<<n_boards, threads, sm, as_stream(stream)>>>(pred, board_conf, trials, hw,
+                                                                   n_cap, src, kept);
+  return cuda_status(cudaGetLastError());
+}
+
+int32_t nca_b200_clone(NcaState* st, const int32_t* src, void* stream) {
+  if (!st || !src) return NCA_ERR_INVALID;
+  const long long n = (long long)st->n_inst * st->hw * (st->channels / 4);
+  const int bs = 256;
+  clone_kernel<<<(unsigned)((n + bs - 1) / bs), bs, 0, as_stream(stream)>>>(
+      st->master[st->cur], st->mirror[st->cur], st->channels, st->hw, st->n_inst, src);
+  return cuda_status(cudaGetLastError());
+}
+
+int32_t nca_b200_ctrl_status(int32_t* ctrl, int32_t* detail, void* stream) {
+  if (!ctrl) return NCA_ERR_INVALID;
+  cudaStream_t s = as_stream(stream);
+  int32_t h[4] = {0, 0, 0, 0};
+  cudaError_t e = cudaMemcpyAsync(h, ctrl, sizeof(h), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return NCA_ERR_CUDA;
+  if (detail) *detail = h[1];
+  if (h[0] != 0) {
+    e = cudaMemsetAsync(ctrl, 0, sizeof(h), s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return NCA_ERR_CUDA;
+    return h[0];
+  }
+  return NCA_OK;
+}
+
+int32_t nca_b200_selftest_timeout(int32_t* ctrl, int32_t timeout_ms, void* stream) {
+  if (!ctrl || timeout_ms <= 0) return NCA_ERR_INVALID;
+  cudaStream_t s = as_stream(stream);
+  cudaError_t e = cudaMemsetAsync(ctrl, 0, 4 * sizeof(int32_t), s);
+  if (e != cudaSuccess) return NCA_ERR_CUDA;
+  selftest_wait_kernel<<<1, 64, 0, s>>>(ctrl, (unsigned long long)timeout_ms * 1000000ull);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return NCA_ERR_CUDA;
+  return nca_b200_ctrl_status(ctrl, nullptr, stream);
+}
+
+}  // extern "C"

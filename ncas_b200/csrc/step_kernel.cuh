@@ -1,0 +1,684 @@
+// step_kernel.cuh -- the persistent NCA step kernel for sm_100a.
+//
+// One CTA per SM.  Each step, every instance's cells are processed in tiles of 128 consecutive
+// cells (global cell index g = inst * H * W + i * W + j).  Per tile:
+//
+//   loader warp    cp.async of the tile's halo window (cells g0-W-1 .. g0+128+W) of the
+//                  previous state into a bank-swizzled shared-memory stage
+//   stencil warps  one thread per tile row: 3x3 perception with zero padding (4 heads, head-major
+//                  z[k*C + c] as nca.model.KernelPerception, src/nca/model.py:175-178), written
+//                  as bf16 (hi, lo) pairs straight into tensor memory: the A operand of GEMM1
+//   MMA thread     GEMM1 acc1 = z W1^T (tcgen05.mma kind::f16, A from TMEM, B = fc1.weight in
+//                  128B-swizzled smem), then after the hidden epilogue GEMM2 acc2 = h W2^T
+//   epilogue warps E1: h = relu(acc1 + b1) -> bf16 back into TMEM (A operand of GEMM2);
+//                  E2: dx = acc2 + b2, fire mask, x' = x + f*dx, clamp, store (src/nca/model.py:
+//                  527-559, 430-438)
+//
+// Tensor memory (512 columns x 128 lanes): NZ slots holding z (then h) and one accumulator
+// region holding acc1 (then acc2 in its first C columns).  Every wait is bounded; a wait that
+// runs out records NCA_ERR_TIMEOUT in the control words and the CTA drains and exits.
+#pragma once
+#include "ptx.cuh"
+
+namespace nca {
+
+constexpr int kTileM = 128;
+constexpr int kNumWarps = 18;       // 0 MMA, 1 loader, 2..9 stencil, 10..17 epilogue
+constexpr int kThreads = kNumWarps * 32;
+constexpr int kStencilWarp0 = 2;
+constexpr int kEpiWarp0 = 10;
+
+constexpr int pow2ceil(int v) {
+  int p = 32;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+template <int C_, int HD_, bool SPLIT_>
+struct StepCfg {
+  static constexpr int C = C_;
+  static constexpr int P = 4 * C_;
+  static constexpr int HD = HD_;
+  static constexpr bool SPLIT = SPLIT_;
+  static constexpr bool SRC_BF16 = !SPLIT_;
+  static constexpr int SRC_BYTES = SRC_BF16 ? 2 : 4;
+  static constexpr int ROWB = C * SRC_BYTES;         // bytes of one cell in a window stage
+  static constexpr int NCH = ROWB / 16;              // 16-byte chunks per cell
+  static constexpr int CPC = 16 / SRC_BYTES;         // channels per chunk
+  static constexpr int ZPARTS = SPLIT ? 2 : 1;
+  static constexpr int KMAX = P > HD ? P : HD;
+  static constexpr int SLOT_COLS = ZPARTS * KMAX / 2;
+  static constexpr int NZ = (2 * SLOT_COLS + HD <= 512) ? 2 : 1;
+  static constexpr int ACC_COL = NZ * SLOT_COLS;
+  static constexpr int TMEM_COLS = pow2ceil(ACC_COL + HD);
+  static constexpr int W1_BYTES = HD * P * 2;
+  static constexpr int W2_BYTES = C * HD * 2;
+  static_assert(ACC_COL + HD <= 512, "tensor memory budget");
+  static_assert(C % 16 == 0 && HD % 32 == 0 && HD <= 256 && P % 64 == 0 && HD % 64 == 0,
+                "shape constraints of the UMMA tiles");
+  static_assert(NCH % 2 == 0, "stencil channel halves");
+};
+
+struct StepArgs {
+  int n_inst, H, W, HW, K;
+  long long total, n_tiles, inst_offset;
+  int n_steps;
+  long long step0;
+  int stages, win_cells;
+  int c_in, in_off, c_out, out_off, n_out, fixed_taps;
+  float taps[4][9];
+  float head_w[16][16];
+  float head_b[16];
+  const uint8_t* wimg;
+  const float* b1;
+  const float* b2;
+  const uint8_t* given;
+  const float* clamp;
+  const int* inst_row;
+  float* master[2];
+  uint16_t* mirror[2];
+  int cur;
+  int fire_mode;
+  float p_fire, ad_scale, ad_bias;
+  unsigned long long seed;
+  const uint8_t* masks;
+  const float* uniforms;
+  unsigned* updates;
+  int* ctrl;
+  unsigned long long timeout_ns;
+};
+
+// Shared-memory layout (offsets from a 1024-byte aligned base).
+template <class Cfg>
+struct SmemLayout {
+  int w1, w2, win, b1, b2, bars, misc, total;
+  __host__ __device__ SmemLayout(int stages, int win_cells) {
+    w1 = 0;
+    w2 = w1 + Cfg::W1_BYTES;
+    win = (w2 + Cfg::W2_BYTES + 1023) & ~1023;
+    b1 = (win + stages * win_cells * Cfg::ROWB + 15) & ~15;
+    b2 = b1 + Cfg::HD * 4;
+    bars = (b2 + Cfg::C * 4 + 7) & ~7;
+    misc = bars + 16 * 8;
+    total = misc + 64;
+  }
+};
+
+enum BarId {
+  BAR_WIN_FULL = 0,   // +stage (2)
+  BAR_WIN_EMPTY = 2,  // +stage (2)
+  BAR_Z_FULL = 4,     // +slot (2)
+  BAR_Z_EMPTY = 6,    // +slot (2)
+  BAR_ACC_FULL = 8,
+  BAR_H_FULL = 9,
+  BAR_ACC2_FULL = 10,
+  BAR_ACC_EMPTY = 11,
+  BAR_WEIGHTS = 12,
+  BAR_DRAIN = 13,
+};
+
+// Failure sites reported in ctrl[1].
+enum Where {
+  W_MMA_ZFULL = 1, W_MMA_ACCEMPTY, W_MMA_HFULL, W_MMA_WEIGHTS, W_LOAD_EMPTY, W_LOAD_GRID,
+  W_ST_WINFULL, W_ST_ZEMPTY, W_E1_ACC, W_E2_ACC2, W_DRAIN
+};
+
+// Bank swizzle of a window stage: 16-byte chunk `ch` of window cell `wc` lives at position
+// ch ^ swz(wc), so that 8 consecutive cells read by 8 lanes hit 8 distinct bank groups.
+template <int NCH>
+__device__ __forceinline__ int win_swz(int wc) {
+  if constexpr (NCH >= 8) return wc & 7;
+  else if constexpr (NCH == 4) return (wc >> 1) & 3;
+  else return (wc >> 2) & 1;
+}
+
+// Warp-converged bounded wait (all 32 lanes call it).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const FailState& fs,
+                                          int where) {
+  const int lane = threadIdx.x & 31;
+  uint64_t start = 0;
+  if (lane == 0) start = global_timer_ns();
+  for (uint32_t it = 0;; ++it) {
+    bool done = mbar_try_wait(bar, parity);
+    if (__all_sync(0xffffffffu, done)) return true;
+    int give_up = 0;
+    if ((it & 63) == 63 && lane == 0) {
+      if (should_abort(fs)) give_up = 1;
+      else if (global_timer_ns() - start > fs.timeout_ns || it > (1u << 28)) {
+        report_failure(fs, 4, where);
+        give_up = 1;
+      }
+    }
+    if (__shfl_sync(0xffffffffu, give_up, 0)) return false;
+    if (it > 128) __nanosleep(32);
+  }
+}
+
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) |   // LBO = 16 B (unused)
+         ((uint64_t)(1024 >> 4) << 32) |                              // SBO = 1024 B
+         ((uint64_t)1 << 46) |                                        // descriptor version
+         ((uint64_t)2 << 61);                                         // SWIZZLE_128B
+}
+
+__device__ __forceinline__ uint32_t idesc_bf16_f32(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+
+// ------------------------------------------------------------------------------------------
+// Stencil of one chunk: fixed identity / Sobel-x / Sobel-y / Laplacian taps.
+//   Sobel-x = [[-1,0,1],[-2,0,2],[-1,0,1]] / 8 (src/nca/model.py:200), Sobel-y = its transpose,
+//   Laplacian = [[1,2,1],[2,-12,2],[1,2,1]] / 16.
+// Neighbours named by position:  a b c / d e f / g h k.
+__device__ __forceinline__ void fixed_taps4(float a, float b, float c, float d, float e, float f,
+                                            float g, float h, float k, float& sx, float& sy,
+                                            float& lap) {
+  float L = fmaf(2.f, d, a) + g;
+  float R = fmaf(2.f, f, c) + k;
+  float T = fmaf(2.f, b, a) + c;
+  float B = fmaf(2.f, h, g) + k;
+  sx = (R - L) * 0.125f;
+  sy = (B - T) * 0.125f;
+  float s = T + B;
+  s = fmaf(2.f, d, s);
+  s = fmaf(2.f, f, s);
+  s = fmaf(-12.f, e, s);
+  lap = s * 0.0625f;
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_constant__ StepArgs A) {
+  using namespace nca;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  const SmemLayout<Cfg> L(A.stages, A.win_cells);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L.misc);
+  int* abort_flag = reinterpret_cast<int*>(smem + L.misc + 8);
+  float* s_b1 = reinterpret_cast<float*>(smem + L.b1);
+  float* s_b2 = reinterpret_cast<float*>(smem + L.b2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  FailState fs;
+  fs.ctrl = A.ctrl;
+  fs.cta_abort = abort_flag;
+  fs.timeout_ns = A.timeout_ns;
+  fs.deadline_ns = 0;
+
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars[BAR_WIN_FULL + s], 32);
+      mbar_init(&bars[BAR_WIN_EMPTY + s], 8);
+      mbar_init(&bars[BAR_Z_FULL + s], 8);
+      mbar_init(&bars[BAR_Z_EMPTY + s], 1);
+    }
+    mbar_init(&bars[BAR_ACC_FULL], 1);
+    mbar_init(&bars[BAR_H_FULL], 8);
+    mbar_init(&bars[BAR_ACC2_FULL], 1);
+    mbar_init(&bars[BAR_ACC_EMPTY], 8);
+    mbar_init(&bars[BAR_WEIGHTS], 1);
+    mbar_init(&bars[BAR_DRAIN], 1);
+    fence_mbar_init();
+  }
+  for (int i = threadIdx.x; i < Cfg::HD; i += kThreads) s_b1[i] = A.b1[i];
+  for (int i = threadIdx.x; i < Cfg::C; i += kThreads) s_b2[i] = A.b2[i];
+  if (warp == 0) {
+    tmem_alloc(tmem_holder, Cfg::TMEM_COLS);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  // A previous launch on this control block failed: do not touch the state.
+  const bool skip = (*((volatile int*)&A.ctrl[0]) != 0);
+
+  const int grid = gridDim.x;
+  const long long total = A.total;
+  const int W = A.W;
+
+  if (!skip && warp == 0) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      bool ok = true;
+      // weights are loaded by the loader warp
+      {
+        uint64_t t0 = global_timer_ns();
+        while (!mbar_try_wait(&bars[BAR_WEIGHTS], 0)) {
+          if (should_abort(fs)) { ok = false; break; }
+          if (global_timer_ns() - t0 > fs.timeout_ns) { report_failure(fs, 4, W_MMA_WEIGHTS); ok = false; break; }
+          __nanosleep(64);
+        }
+      }
+      const uint32_t w1 = smem_u32(smem + L.w1);
+      const uint32_t w2 = smem_u32(smem + L.w2);
+      const uint32_t id1 = idesc_bf16_f32(kTileM, Cfg::HD);
+      const uint32_t id2 = idesc_bf16_f32(kTileM, Cfg::C);
+      long long it = 0;
+      for (int s = 0; ok && s < A.n_steps; ++s) {
+        for (long long t = blockIdx.x; ok && t < A.n_tiles; t += grid, ++it) {
+          const int slot = (int)(it % Cfg::NZ);
+          const uint32_t u = (uint32_t)(it / Cfg::NZ);
+          const uint32_t zcol = tmem + slot * Cfg::SLOT_COLS;
+          if (!mbar_wait(&bars[BAR_Z_FULL + slot], u & 1, fs, W_MMA_ZFULL)) { ok = false; break; }
+          if (!mbar_wait(&bars[BAR_ACC_EMPTY], ((uint32_t)it & 1) ^ 1, fs, W_MMA_ACCEMPTY)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll 1
+          for (int kk = 0; kk < Cfg::P / 16; ++kk) {
+            const uint64_t bd = umma_desc_sw128(w1 + (kk >> 2) * (Cfg::HD * 128) + (kk & 3) * 32);
+#pragma unroll
+            for (int part = 0; part < Cfg::ZPARTS; ++part)
+              umma_bf16_ts(tmem + Cfg::ACC_COL, zcol + part * (Cfg::P / 2) + kk * 8, bd, id1,
+                           (kk | part) != 0);
+          }
+          umma_commit(&bars[BAR_ACC_FULL]);
+          if (!mbar_wait(&bars[BAR_H_FULL], (uint32_t)it & 1, fs, W_MMA_HFULL)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll 1
+          for (int kk = 0; kk < Cfg::HD / 16; ++kk) {
+            const uint64_t bd = umma_desc_sw128(w2 + (kk >> 2) * (Cfg::C * 128) + (kk & 3) * 32);
+#pragma unroll
+            for (int part = 0; part < Cfg::ZPARTS; ++part)
+              umma_bf16_ts(tmem + Cfg::ACC_COL, zcol + part * (Cfg::HD / 2) + kk * 8, bd, id2,
+                           (kk | part) != 0);
+          }
+          umma_commit(&bars[BAR_ACC2_FULL]);
+          umma_commit(&bars[BAR_Z_EMPTY + slot]);
+        }
+      }
+      // Drain: every MMA issued above has completed once this commit arrives.
+      umma_commit(&bars[BAR_DRAIN]);
+      uint64_t t0 = global_timer_ns();
+      while (!mbar_try_wait(&bars[BAR_DRAIN], 0)) {
+        if (global_timer_ns() - t0 > fs.timeout_ns) { report_failure(fs, 4, W_DRAIN); break; }
+        __nanosleep(64);
+      }
+    }
+    __syncwarp();
+  } else if (!skip && warp == 1) {
+    // ---------------------------------------------------------------- loader
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bars[BAR_WEIGHTS], Cfg::W1_BYTES + Cfg::W2_BYTES);
+      const uint32_t dst = smem_u32(smem + L.w1);
+      const int tot = Cfg::W1_BYTES + Cfg::W2_BYTES;   // w1 and w2 are contiguous in smem
+      for (int off = 0; off < tot; off += 16384) {
+        const int n = (tot - off) < 16384 ? (tot - off) : 16384;
+        bulk_g2s(dst + off, A.wimg + off, n, &bars[BAR_WEIGHTS]);
+      }
+    }
+    __syncwarp();
+    const int NCH = Cfg::NCH;
+    const int WC = A.win_cells;
+    const int S = A.stages;
+    long long it = 0;
+    bool ok = true;
+    for (int s = 0; ok && s < A.n_steps; ++s) {
+      const int in = (A.cur + s) & 1;
+      const uint8_t* src = Cfg::SRC_BF16 ? reinterpret_cast<const uint8_t*>(A.mirror[in])
+                                         : reinterpret_cast<const uint8_t*>(A.master[in]);
+      if (s > 0) {
+        // grid barrier: every CTA has stored its tiles of step s-1
+        int give_up = 0;
+        if (lane == 0) {
+          const unsigned target = (unsigned)s * (unsigned)grid;
+          uint64_t t0 = global_timer_ns();
+          for (uint32_t k = 0;; ++k) {
+            unsigned v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(&A.ctrl[2]) : "memory");
+            if (v >= target) break;
+            if (should_abort(fs)) { give_up = 1; break; }
+            if (global_timer_ns() - t0 > fs.timeout_ns || k > (1u << 28)) {
+              report_failure(fs, 4, W_LOAD_GRID);
+              give_up = 1;
+              break;
+            }
+            __nanosleep(128);
+          }
+        }
+        if (__shfl_sync(0xffffffffu, give_up, 0)) { ok = false; break; }
+      }
+      for (long long t = blockIdx.x; t < A.n_tiles; t += grid, ++it) {
+        const int stage = (int)(it % S);
+        const uint32_t v = (uint32_t)(it / S);
+        if (!warp_wait(&bars[BAR_WIN_EMPTY + stage], (v & 1) ^ 1, fs, W_LOAD_EMPTY)) { ok = false; break; }
+        const long long wb = t * kTileM - W - 1;
+        const uint32_t dst = smem_u32(smem + L.win + stage * WC * Cfg::ROWB);
+        for (int idx = lane; idx < WC * NCH; idx += 32) {
+          const int ch = idx / WC;
+          const int wc = idx - ch * WC;
+          const long long gs = wb + wc;
+          const bool in_range = gs >= 0 && gs < total;
+          const long long gcl = in_range ? gs : 0;
+          const uint8_t* p = src + ((((gcl >> 7) * NCH + ch) << 7) + (gcl & 127)) * 16;
+          cp_async_16(dst + wc * Cfg::ROWB + ((ch ^ win_swz<Cfg::NCH>(wc)) << 4), p,
+                      in_range ? 16u : 0u);
+        }
+        cp_async_mbar_arrive_noinc(&bars[BAR_WIN_FULL + stage]);
+      }
+    }
+    cp_async_wait_all();
+    __syncwarp();
+  } else if (!skip && warp >= kStencilWarp0 && warp < kEpiWarp0) {
+    // ---------------------------------------------------------------- stencil
+    const int sw = warp - kStencilWarp0;
+    const int half = sw >> 2;
+    const int quarter = warp & 3;
+    const int m = quarter * 32 + lane;     // tile row = TMEM lane
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    const int WC = A.win_cells;
+    const int S = A.stages;
+    long long it = 0;
+    bool ok = true;
+    for (int s = 0; ok && s < A.n_steps; ++s) {
+      for (long long t = blockIdx.x; t < A.n_tiles; t += grid, ++it) {
+        const int stage = (int)(it % S);
+        const uint32_t v = (uint32_t)(it / S);
+        const int slot = (int)(it % Cfg::NZ);
+        const uint32_t u = (uint32_t)(it / Cfg::NZ);
+        if (!warp_wait(&bars[BAR_WIN_FULL + stage], v & 1, fs, W_ST_WINFULL)) { ok = false; break; }
+        if (!warp_wait(&bars[BAR_Z_EMPTY + slot], (u & 1) ^ 1, fs, W_ST_ZEMPTY)) { ok = false; break; }
+        tc_fence_after();
+        const uint8_t* win = smem + L.win + stage * WC * Cfg::ROWB;
+        const long long g = t * kTileM + m;
+        const bool valid = g < total;
+        int i = 0, j = 0;
+        if (valid) {
+          const int p = (int)(g % A.HW);
+          i = p / W;
+          j = p - i * W;
+        }
+        const bool up = valid && i > 0, dn = valid && i < A.H - 1;
+        const bool lf = valid && j > 0, rt = valid && j < W - 1;
+        const int c0 = m + W + 1;  // window index of this cell
+        const uint32_t zbase = tmem + lane_addr + slot * Cfg::SLOT_COLS;
+#pragma unroll 1
+        for (int q = 0; q < Cfg::NCH / 2; ++q) {
+          const int ch = half * (Cfg::NCH / 2) + q;
+          auto ld = [&](bool ok_, int wc) -> uint4 {
+            uint4 r = make_uint4(0u, 0u, 0u, 0u);
+            if (ok_) r = *reinterpret_cast<const uint4*>(win + wc * Cfg::ROWB + ((ch ^ win_swz<Cfg::NCH>(wc)) << 4));
+            return r;
+          };
+          const uint4 va = ld(up && lf, c0 - W - 1), vb = ld(up, c0 - W), vc = ld(up && rt, c0 - W + 1);
+          const uint4 vd = ld(lf, c0 - 1), ve = ld(valid, c0), vf = ld(rt, c0 + 1);
+          const uint4 vg = ld(dn && lf, c0 + W - 1), vh = ld(dn, c0 + W), vk = ld(dn && rt, c0 + W + 1);
+          if constexpr (Cfg::SRC_BF16) {
+            // 8 channels: ch*8 .. ch*8+7
+            const uint32_t* A_ = &va.x; const uint32_t* B_ = &vb.x; const uint32_t* C_ = &vc.x;
+            const uint32_t* D_ = &vd.x; const uint32_t* E_ = &ve.x; const uint32_t* F_ = &vf.x;
+            const uint32_t* G_ = &vg.x; const uint32_t* H_ = &vh.x; const uint32_t* K_ = &vk.x;
+            uint32_t zi[4], zx[4], zy[4], zl[4];
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+              float o[2][3];
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                auto cv = [&](uint32_t x) { return e == 0 ? bf16lo_to_f32(x) : bf16hi_to_f32(x); };
+                if (A.fixed_taps) {
+                  fixed_taps4(cv(A_[w]), cv(B_[w]), cv(C_[w]), cv(D_[w]), cv(E_[w]), cv(F_[w]),
+                              cv(G_[w]), cv(H_[w]), cv(K_[w]), o[e][0], o[e][1], o[e][2]);
+                } else {
+                  const float nb[9] = {cv(A_[w]), cv(B_[w]), cv(C_[w]), cv(D_[w]), cv(E_[w]),
+                                       cv(F_[w]), cv(G_[w]), cv(H_[w]), cv(K_[w])};
+#pragma unroll
+                  for (int kh = 1; kh < 4; ++kh) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int n = 0; n < 9; ++n) acc = fmaf(A.taps[kh][n], nb[n], acc);
+                    o[e][kh - 1] = acc;
+                  }
+                }
+              }
+              if (A.fixed_taps) {
+                zi[w] = E_[w];  // identity head of a bf16 source is the value itself
+              } else {
+                const float nb0[9] = {bf16lo_to_f32(A_[w]), bf16lo_to_f32(B_[w]), bf16lo_to_f32(C_[w]),
+                                      bf16lo_to_f32(D_[w]), bf16lo_to_f32(E_[w]), bf16lo_to_f32(F_[w]),
+                                      bf16lo_to_f32(G_[w]), bf16lo_to_f32(H_[w]), bf16lo_to_f32(K_[w])};
+                const float nb1[9] = {bf16hi_to_f32(A_[w]), bf16hi_to_f32(B_[w]), bf16hi_to_f32(C_[w]),
+                                      bf16hi_to_f32(D_[w]), bf16hi_to_f32(E_[w]), bf16hi_to_f32(F_[w]),
+                                      bf16hi_to_f32(G_[w]), bf16hi_to_f32(H_[w]), bf16hi_to_f32(K_[w])};
+                float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+                for (int n = 0; n < 9; ++n) { a0 = fmaf(A.taps[0][n], nb0[n], a0); a1 = fmaf(A.taps[0][n], nb1[n], a1); }
+                zi[w] = pack_bf16(a0, a1);
+              }
+              zx[w] = pack_bf16(o[0][0], o[1][0]);
+              zy[w] = pack_bf16(o[0][1], o[1][1]);
+              zl[w] = pack_bf16(o[0][2], o[1][2]);
+            }
+            const int cb = ch * 8;  // first channel of the chunk
+            tmem_st4(zbase + (0 * Cfg::C + cb) / 2, zi);
+            tmem_st4(zbase + (1 * Cfg::C + cb) / 2, zx);
+            tmem_st4(zbase + (2 * Cfg::C + cb) / 2, zy);
+            tmem_st4(zbase + (3 * Cfg::C + cb) / 2, zl);
+          } else {
+            // fp32 source, 4 channels: ch*4 .. ch*4+3; z split into bf16 hi + lo parts
+            const float* A_ = reinterpret_cast<const float*>(&va); const float* B_ = reinterpret_cast<const float*>(&vb);
+            const float* C_ = reinterpret_cast<const float*>(&vc); const float* D_ = reinterpret_cast<const float*>(&vd);
+            const float* E_ = reinterpret_cast<const float*>(&ve); const float* F_ = reinterpret_cast<const float*>(&vf);
+            const float* G_ = reinterpret_cast<const float*>(&vg); const float* H_ = reinterpret_cast<const float*>(&vh);
+            const float* K_ = reinterpret_cast<const float*>(&vk);
+            float z[4][4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              if (A.fixed_taps) {
+                z[0][e] = E_[e];
+                fixed_taps4(A_[e], B_[e], C_[e], D_[e], E_[e], F_[e], G_[e], H_[e], K_[e], z[1][e],
+                            z[2][e], z[3][e]);
+              } else {
+                const float nb[9] = {A_[e], B_[e], C_[e], D_[e], E_[e], F_[e], G_[e], H_[e], K_[e]};
+#pragma unroll
+                for (int kh = 0; kh < 4; ++kh) {
+                  float acc = 0.f;
+#pragma unroll
+                  for (int n = 0; n < 9; ++n) acc = fmaf(A.taps[kh][n], nb[n], acc);
+                  z[kh][e] = acc;
+                }
+              }
+            }
+            const int cb = ch * 4;
+#pragma unroll
+            for (int kh = 0; kh < 4; ++kh) {
+              const uint32_t h01 = pack_bf16(z[kh][0], z[kh][1]);
+              const uint32_t h23 = pack_bf16(z[kh][2], z[kh][3]);
+              const uint32_t l01 = pack_bf16(z[kh][0] - bf16lo_to_f32(h01), z[kh][1] - bf16hi_to_f32(h01));
+              const uint32_t l23 = pack_bf16(z[kh][2] - bf16lo_to_f32(h23), z[kh][3] - bf16hi_to_f32(h23));
+              const uint32_t col = (kh * Cfg::C + cb) / 2;
+              tmem_st2(zbase + col, h01, h23);
+              tmem_st2(zbase + Cfg::P / 2 + col, l01, l23);
+            }
+          }
+        }
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&bars[BAR_Z_FULL + slot]);
+          mbar_arrive(&bars[BAR_WIN_EMPTY + stage]);
+        }
+      }
+    }
+  } else if (!skip && warp >= kEpiWarp0) {
+    // ---------------------------------------------------------------- epilogue
+    const int ew = warp - kEpiWarp0;
+    const int half = ew >> 2;
+    const int quarter = warp & 3;
+    const int m = quarter * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    constexpr int CH = Cfg::C / 2;          // channels of this thread in E2
+    long long it = 0;
+    bool ok = true;
+    for (int s = 0; ok && s < A.n_steps; ++s) {
+      const int in = (A.cur + s) & 1;
+      const int out = in ^ 1;
+      const float* xin = A.master[in];
+      float* xout = A.master[out];
+      uint16_t* mout = A.mirror[out];
+      const long long step = A.step0 + s;
+      for (long long t = blockIdx.x; t < A.n_tiles; t += grid, ++it) {
+        const int slot = (int)(it % Cfg::NZ);
+        const uint32_t zbase = tmem + lane_addr + slot * Cfg::SLOT_COLS;
+        const uint32_t abase = tmem + lane_addr + Cfg::ACC_COL;
+        // ---- E1: hidden = relu(acc1 + b1) -> bf16 into the z slot
+        if (!warp_wait(&bars[BAR_ACC_FULL], (uint32_t)it & 1, fs, W_E1_ACC)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll 1
+        for (int cbk = 0; cbk < Cfg::HD / 2; cbk += 32) {
+          const int col = half * (Cfg::HD / 2) + cbk;
+          uint32_t r[32];
+          tmem_ld32(abase + col, r);
+          tc_wait_ld();
+          uint32_t hi[16];
+          if constexpr (!Cfg::SPLIT) {
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+              hi[q] = pack_bf16_relu(__uint_as_float(r[2 * q]) + s_b1[col + 2 * q],
+                                     __uint_as_float(r[2 * q + 1]) + s_b1[col + 2 * q + 1]);
+            tmem_st16(zbase + col / 2, hi);
+          } else {
+            uint32_t lo[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+              const float h0 = fmaxf(__uint_as_float(r[2 * q]) + s_b1[col + 2 * q], 0.f);
+              const float h1 = fmaxf(__uint_as_float(r[2 * q + 1]) + s_b1[col + 2 * q + 1], 0.f);
+              hi[q] = pack_bf16(h0, h1);
+              lo[q] = pack_bf16(h0 - bf16lo_to_f32(hi[q]), h1 - bf16hi_to_f32(hi[q]));
+            }
+            tmem_st16(zbase + col / 2, hi);
+            tmem_st16(zbase + Cfg::HD / 2 + col / 2, lo);
+          }
+        }
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[BAR_H_FULL]);
+
+        // ---- E2: dx = acc2 + b2; x' = x + f * dx; clamp; store
+        const long long g = t * kTileM + m;
+        const bool valid = g < total;
+        int inst = 0, p = 0, row = 0;
+        if (valid) {
+          inst = (int)(g / A.HW);
+          p = (int)(g - (long long)inst * A.HW);
+          row = A.inst_row ? A.inst_row[inst] : inst / A.K;
+        }
+        // fire decision (needs the old state for the adaptive rule)
+        float f = 0.f;
+        if (valid) {
+          if (A.fire_mode == 0) {
+            f = A.masks[((long long)s * A.n_inst + inst) * A.HW + p] ? 1.f : 0.f;
+          } else {
+            float prob = A.p_fire;
+            if (A.fire_mode >= 2) {
+              float xo[16];
+              for (int c = 0; c < A.c_out; ++c) {
+                const int cc = A.out_off + c;
+                xo[c] = xin[(((t * (Cfg::C / 4) + (cc >> 2)) << 7) + m) * 4 + (cc & 3)];
+              }
+              float sc[16];
+              float mx = -3.402823466e38f;
+              for (int o = 0; o < A.n_out; ++o) {
+                float a = A.head_b[o];
+                for (int c = 0; c < A.c_out; ++c) a = fmaf(A.head_w[o][c], xo[c], a);
+                sc[o] = a;
+                mx = fmaxf(mx, a);
+              }
+              float den = 0.f;
+              for (int o = 0; o < A.n_out; ++o) den += expf(sc[o] - mx);
+              float conf = fminf(fmaxf(1.f / den, 0.f), 1.f);
+              prob = A.ad_scale * (1.f - conf) + A.ad_bias;
+            }
+            float uu;
+            if (A.fire_mode == 3) uu = A.uniforms[((long long)s * A.n_inst + inst) * A.HW + p];
+            else uu = philox_uniform(A.seed, A.inst_offset + inst, p, step);
+            f = (uu < prob) ? 1.f : 0.f;
+          }
+        }
+        if (!warp_wait(&bars[BAR_ACC2_FULL], (uint32_t)it & 1, fs, W_E2_ACC2)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t r[CH];
+        if constexpr (CH == 32) {
+          tmem_ld32(abase + half * CH, r);
+        } else {
+          tmem_ld16(abase + half * CH, *reinterpret_cast<uint32_t(*)[16]>(r));
+        }
+        tc_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[BAR_ACC_EMPTY]);
+        if (valid) {
+          const bool gv = A.given[(long long)row * A.HW + p] != 0;
+          const float* clamp_row = A.clamp + ((long long)row * A.HW + p) * A.c_in;
+#pragma unroll
+          for (int q = 0; q < CH / 8; ++q) {
+            float xn[8];
+#pragma unroll
+            for (int hq = 0; hq < 2; ++hq) {
+              const int c4 = (half * CH) / 4 + q * 2 + hq;   // float4 chunk index
+              const float4 xo = *reinterpret_cast<const float4*>(xin + (((t * (Cfg::C / 4) + c4) << 7) + m) * 4);
+              const float xv[4] = {xo.x, xo.y, xo.z, xo.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int c = c4 * 4 + e;
+                const float dx = __uint_as_float(r[q * 8 + hq * 4 + e]) + s_b2[c];
+                float y = fmaf(f, dx, xv[e]);
+                const int ci = c - A.in_off;
+                if (gv && ci >= 0 && ci < A.c_in) y = clamp_row[ci];
+                xn[hq * 4 + e] = y;
+              }
+              *reinterpret_cast<float4*>(xout + (((t * (Cfg::C / 4) + c4) << 7) + m) * 4) =
+                  make_float4(xn[hq * 4 + 0], xn[hq * 4 + 1], xn[hq * 4 + 2], xn[hq * 4 + 3]);
+            }
+            if constexpr (Cfg::SRC_BF16) {
+              const int c8 = (half * CH) / 8 + q;
+              uint4 pk;
+              pk.x = pack_bf16(xn[0], xn[1]);
+              pk.y = pack_bf16(xn[2], xn[3]);
+              pk.z = pack_bf16(xn[4], xn[5]);
+              pk.w = pack_bf16(xn[6], xn[7]);
+              *reinterpret_cast<uint4*>(mout + (((t * (Cfg::C / 8) + c8) << 7) + m) * 8) = pk;
+            }
+          }
+        }
+        if (half == 0 && A.updates != nullptr) {
+          const bool fired = valid && f > 0.f;
+          const unsigned grp = __match_any_sync(0xffffffffu, valid ? inst : -1);
+          const unsigned fm = __ballot_sync(0xffffffffu, fired);
+          if (valid && lane == __ffs(grp) - 1) {
+            const int cnt = __popc(fm & grp);
+            if (cnt) atomicAdd(&A.updates[inst], (unsigned)cnt);
+          }
+        }
+      }
+      // Step done: this CTA's stores of step s are complete.  The barrier also ORs the failure
+      // flags of the 8 epilogue warps so that they leave the step loop together.
+      unsigned any_fail;
+      asm volatile(
+          "{\n\t.reg .pred p, q;\n\t"
+          "setp.ne.u32 p, %1, 0;\n\t"
+          "bar.red.or.pred q, 1, 256, p;\n\t"
+          "selp.u32 %0, 1, 0, q;\n\t}"
+          : "=r"(any_fail)
+          : "r"((unsigned)(!ok || *(volatile int*)abort_flag != 0))
+          : "memory");
+      if (any_fail) { ok = false; break; }
+      if (threadIdx.x == kEpiWarp0 * 32) {
+        __threadfence();
+        atomicAdd(reinterpret_cast<unsigned*>(&A.ctrl[2]), 1u);
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace nca

@@ -1,0 +1,386 @@
+"""Host side of the B200 rollout: weights, batches, states and calls into libnca_b200.
+
+`B200Engine` takes any model object with the reference's layout (nca.model.NCA or
+ncas_b200.model.NCA): `cfg`, `perceive.weight`, `update.fc1/fc2`, `head`.  It packs the MLP
+weights once into the bf16 shared-memory image the tcgen05 kernels read, and exposes the
+operations of the rollout path on device tensors.  All compute is done by the library; torch
+provides device memory, the current CUDA stream and host<->device copies.
+
+`B200RolloutBlocks` is the drop-in for nca.engine.inference.UniformRolloutBlocks
+(src/nca/engine/inference.py:79-104): same constructor shape and `__call__(x, given4, clamp,
+fires, noises)`, selected in the reference's rollout by RolloutConfig.engine.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from .model import FIXED_TAPS, check_supported
+
+# Limit of any single wait inside a kernel (a grid barrier, a pipeline handoff).
+DEFAULT_TIMEOUT_MS = int(os.environ.get("NCA_B200_TIMEOUT_MS", "20000"))
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+@dataclass
+class Batch:
+    """Device arrays of one batch of instances plus its NcaBatchDesc."""
+
+    desc: L.NcaBatchDesc
+    n_inst: int
+    height: int
+    width: int
+    trials: int
+    given: torch.Tensor   # (rows, H*W) uint8
+    clamp: torch.Tensor   # (rows, H*W, c_in) fp32
+    inputs: torch.Tensor  # (rows, H*W) uint8
+    inst_row: torch.Tensor | None
+
+    @property
+    def hw(self) -> int:
+        return self.height * self.width
+
+
+class State:
+    """An NcaState workspace (ping-pong tiled fp32 state, bf16 mirror) owned by torch."""
+
+    def __init__(self, engine: B200Engine, n_inst: int, hw: int):
+        lib = L.lib()
+        nbytes = C.c_size_t(0)
+        L.check(
+            lib.nca_b200_state_bytes(n_inst, hw, engine.channels, engine.prec, C.byref(nbytes)),
+            "nca_b200_state_bytes",
+        )
+        self.buffer = torch.empty(int(nbytes.value) + 256, dtype=torch.uint8, device=engine.device)
+        base = (self.buffer.data_ptr() + 255) & ~255
+        self.st = L.NcaState()
+        L.check(
+            lib.nca_b200_state_bind(
+                C.byref(self.st), base, nbytes.value, n_inst, hw, engine.channels, engine.prec
+            ),
+            "nca_b200_state_bind",
+        )
+        self.n_inst, self.hw = n_inst, hw
+
+
+class B200Engine:
+    """Weights and library calls of one model on one CUDA device."""
+
+    def __init__(self, model, precision: str = "bf16", device: torch.device | None = None):
+        cfg = model.cfg
+        check_supported(cfg)
+        if precision not in ("bf16", "split"):
+            raise ValueError("precision must be 'bf16' or 'split'")
+        self.cfg = cfg
+        self.precision = precision
+        self.prec = L.PREC_BF16 if precision == "bf16" else L.PREC_SPLIT
+        w1 = model.update.fc1.weight
+        self.device = torch.device(device) if device is not None else w1.device
+        if self.device.type != "cuda":
+            raise RuntimeError("the b200 backend runs on a CUDA device (no CPU fallback)")
+        lib = L.lib()
+        self.channels = C_ = cfg.channels
+        P = cfg.heads * C_
+        Hd = model.update.fc1.weight.shape[0]
+        self.hidden = Hd
+        w1h = w1.detach().float().reshape(Hd, P).cpu().contiguous().numpy()
+        w2h = model.update.fc2.weight.detach().float().reshape(C_, Hd).cpu().contiguous().numpy()
+        nbytes = C.c_size_t(0)
+        L.check(lib.nca_b200_weights_bytes(C_, P, Hd, C.byref(nbytes)), "nca_b200_weights_bytes")
+        img = np.zeros(int(nbytes.value), dtype=np.uint8)
+        L.check(
+            lib.nca_b200_pack_weights(w1h.ctypes.data, w2h.ctypes.data, C_, P, Hd, img.ctypes.data),
+            "nca_b200_pack_weights",
+        )
+        self.wimg = torch.from_numpy(img).to(self.device)
+        self.b1 = model.update.fc1.bias.detach().float().contiguous().to(self.device)
+        self.b2 = model.update.fc2.bias.detach().float().contiguous().to(self.device)
+        taps = model.perceive.weight.detach().float().reshape(4, 9).cpu().numpy()
+        hw_ = model.head.weight.detach().float().reshape(len(cfg.output_tokens), cfg.c_out).cpu().numpy()
+        hb = model.head.bias.detach().float().cpu().numpy()
+        d = L.NcaModelDesc()
+        d.channels, d.perception, d.hidden = C_, P, Hd
+        d.c_in, d.in_offset, d.c_out, d.out_offset = cfg.c_in, cfg.in_offset, cfg.c_out, cfg.out_offset
+        d.n_out = len(cfg.output_tokens)
+        d.fixed_taps = int(np.array_equal(taps.reshape(4, 3, 3), FIXED_TAPS))
+        for k in range(4):
+            for n in range(9):
+                d.taps[k][n] = float(taps[k, n])
+        for o in range(d.n_out):
+            d.head_b[o] = float(hb[o])
+            d.out_tokens[o] = int(cfg.output_tokens[o])
+            for c in range(cfg.c_out):
+                d.head_w[o][c] = float(hw_[o, c])
+        d.weights = self.wimg.data_ptr()
+        d.b1 = self.b1.data_ptr()
+        d.b2 = self.b2.data_ptr()
+        self.desc = d
+        self.embed = model.embed.detach().float().to(self.device) if hasattr(model, "embed") else None
+        self.ctrl = torch.zeros(4, dtype=torch.int32, device=self.device)
+        self.timeout_ms = DEFAULT_TIMEOUT_MS
+        self.launches = 0  # library kernel launches issued by this engine
+
+    # ------------------------------------------------------------------ batches and states
+    def make_batch(
+        self,
+        given: torch.Tensor,
+        clamp: torch.Tensor,
+        inputs: torch.Tensor,
+        trials: int,
+        n_inst: int | None = None,
+        inst_offset: int = 0,
+        inst_row: torch.Tensor | None = None,
+    ) -> Batch:
+        """given (rows, H, W) bool/uint8, clamp (rows, H, W, c_in) fp32, inputs (rows, H, W)
+        tokens; instance i uses row inst_row[i] or i // trials."""
+        rows, H, W = given.shape
+        dev = self.device
+        g = given.to(dev, torch.uint8).reshape(rows, H * W).contiguous()
+        c = clamp.to(dev, torch.float32).reshape(rows, H * W, self.cfg.c_in).contiguous()
+        x = inputs.to(dev, torch.uint8).reshape(rows, H * W).contiguous()
+        n = rows * trials if n_inst is None else n_inst
+        ir = None if inst_row is None else inst_row.to(dev, torch.int32).contiguous()
+        d = L.NcaBatchDesc()
+        d.n_inst, d.height, d.width, d.trials = n, H, W, trials
+        d.inst_offset = int(inst_offset)
+        d.given, d.clamp, d.inputs = g.data_ptr(), c.data_ptr(), x.data_ptr()
+        d.inst_row = _ptr(ir)
+        return Batch(d, n, H, W, trials, g, c, x, ir)
+
+    def batch_from_boards(self, inputs_np: np.ndarray, given_np: np.ndarray, trials: int,
+                          inst_offset: int = 0) -> Batch:
+        """Boards (N, H, W) tokens / given on the host -> batch of N * trials instances."""
+        if self.embed is None:
+            raise ValueError("the model has no token embedding")
+        inputs = torch.from_numpy(np.ascontiguousarray(inputs_np)).to(self.device)
+        given = torch.from_numpy(np.ascontiguousarray(given_np)).to(self.device)
+        clamp = self.embed[inputs]  # (N, H, W, c_in) embedding lookup of the input tokens
+        return self.make_batch(given, clamp, inputs, trials, inst_offset=inst_offset)
+
+    def new_state(self, n_inst: int, hw: int) -> State:
+        return State(self, n_inst, hw)
+
+    def _s(self) -> int:
+        return _stream(self.device)
+
+    def init_state(self, st: State, b: Batch) -> None:
+        L.check(L.lib().nca_b200_state_init(C.byref(st.st), C.byref(self.desc), C.byref(b.desc), self._s()),
+                "nca_b200_state_init")
+        self.launches += 1
+
+    def load_nchw(self, st: State, x: torch.Tensor) -> None:
+        x = x.to(self.device, torch.float32).contiguous()
+        L.check(L.lib().nca_b200_state_load_nchw(C.byref(st.st), x.data_ptr(), self._s()),
+                "nca_b200_state_load_nchw")
+        self.launches += 1
+
+    def store_nchw(self, st: State, out: torch.Tensor | None = None) -> torch.Tensor:
+        H_W = st.hw
+        if out is None:
+            out = torch.empty((st.n_inst, self.channels, H_W), dtype=torch.float32, device=self.device)
+        L.check(L.lib().nca_b200_state_store_nchw(C.byref(st.st), out.data_ptr(), self._s()),
+                "nca_b200_state_store_nchw")
+        self.launches += 1
+        return out
+
+    # ------------------------------------------------------------------------- the steps
+    def run(
+        self,
+        st: State,
+        b: Batch,
+        n_steps: int,
+        mode: str = "philox",
+        p_fire: float = 0.5,
+        seed: int = 0,
+        step0: int = 0,
+        masks: torch.Tensor | None = None,
+        uniforms: torch.Tensor | None = None,
+        adaptive: tuple[float, float] = (0.9, 0.1),
+        updates: torch.Tensor | None = None,
+    ) -> None:
+        """n_steps NCA steps.  mode: 'mask' (masks (n_steps, n_inst, H*W) uint8), 'philox',
+        'adaptive' (Philox, p = a * (1 - conf) + b) or 'adaptive_uniform' (uniforms given)."""
+        f = L.NcaFireDesc()
+        f.mode = {"mask": L.FIRE_MASK, "philox": L.FIRE_PHILOX, "adaptive": L.FIRE_ADAPTIVE_PHILOX,
+                  "adaptive_uniform": L.FIRE_ADAPTIVE_UNIFORM}[mode]
+        f.p_fire = float(p_fire)
+        f.adapt_scale, f.adapt_bias = float(adaptive[0]), float(adaptive[1])
+        f.seed = int(seed) & ((1 << 64) - 1)
+        f.step0 = int(step0)
+        keep = []
+        if masks is not None:
+            m = masks.to(self.device, torch.uint8).contiguous()
+            assert m.numel() == n_steps * b.n_inst * b.hw, "masks must be (n_steps, n_inst, H*W)"
+            keep.append(m)
+            f.masks = m.data_ptr()
+        if uniforms is not None:
+            u = uniforms.to(self.device, torch.float32).contiguous()
+            assert u.numel() == n_steps * b.n_inst * b.hw
+            keep.append(u)
+            f.uniforms = u.data_ptr()
+        if updates is not None:
+            assert updates.dtype == torch.int32 and updates.numel() >= b.n_inst
+            f.updates = updates.data_ptr()
+        L.check(
+            L.lib().nca_b200_run_steps(
+                C.byref(self.desc), C.byref(b.desc), C.byref(st.st), int(n_steps), C.byref(f),
+                self.ctrl.data_ptr(), int(self.timeout_ms), self._s()
+            ),
+            "nca_b200_run_steps",
+        )
+        self.launches += 2  # control-word reset + step kernel
+        self._keep = keep  # alive until the next call (the kernel reads them asynchronously)
+
+    def check(self) -> None:
+        """Synchronise and raise if a kernel reported a failure in the control words."""
+        detail = C.c_int32(0)
+        s = L.lib().nca_b200_ctrl_status(self.ctrl.data_ptr(), C.byref(detail), self._s())
+        if s != L.NCA_OK:
+            raise L.NcaError(s, "kernel", detail.value)
+
+    # ------------------------------------------------------------------ readout and selection
+    def readout(self, st: State, b: Batch, targets: torch.Tensor | None = None,
+                want_pred: bool = True, want_cell_conf: bool = False) -> dict[str, torch.Tensor]:
+        n, hw = b.n_inst, b.hw
+        dev = self.device
+        out = {"board_conf": torch.empty(n, dtype=torch.float32, device=dev)}
+        if want_pred:
+            out["pred"] = torch.empty((n, hw), dtype=torch.uint8, device=dev)
+        if want_cell_conf:
+            out["cell_conf"] = torch.empty((n, hw), dtype=torch.float32, device=dev)
+        tg = None
+        if targets is not None:
+            tg = targets.to(dev, torch.uint8).reshape(-1, hw).contiguous()
+            out["cell_acc"] = torch.empty(n, dtype=torch.float32, device=dev)
+            out["exact"] = torch.empty(n, dtype=torch.uint8, device=dev)
+        L.check(
+            L.lib().nca_b200_readout(
+                C.byref(self.desc), C.byref(b.desc), C.byref(st.st), _ptr(out.get("pred")),
+                _ptr(out.get("cell_conf")), out["board_conf"].data_ptr(), _ptr(tg),
+                _ptr(out.get("cell_acc")), _ptr(out.get("exact")), self._s()
+            ),
+            "nca_b200_readout",
+        )
+        self.launches += 1
+        return out
+
+    def select(self, board_conf: torch.Tensor, n_boards: int, trials: int, k_limit: int | None = None,
+               alive: torch.Tensor | None = None, pred: torch.Tensor | None = None, hw: int = 0):
+        dev = self.device
+        idx = torch.empty(n_boards, dtype=torch.int32, device=dev)
+        best = torch.empty(n_boards, dtype=torch.float32, device=dev)
+        bp = torch.empty((n_boards, hw), dtype=torch.uint8, device=dev) if pred is not None else None
+        al = None if alive is None else alive.to(dev, torch.uint8).contiguous()
+        L.check(
+            L.lib().nca_b200_select(
+                board_conf.data_ptr(), _ptr(al), n_boards, trials, int(k_limit or trials),
+                idx.data_ptr(), best.data_ptr(), _ptr(pred), hw, _ptr(bp), self._s()
+            ),
+            "nca_b200_select",
+        )
+        self.launches += 1
+        return idx, best, bp
+
+    def prune_refill(self, st: State, pred: torch.Tensor, board_conf: torch.Tensor, n_boards: int,
+                     trials: int, n_cap: int):
+        dev = self.device
+        src = torch.empty(n_boards * trials, dtype=torch.int32, device=dev)
+        kept = torch.empty(n_boards * trials, dtype=torch.uint8, device=dev)
+        L.check(
+            L.lib().nca_b200_prune_refill(
+                pred.data_ptr(), board_conf.data_ptr(), n_boards, trials, pred.shape[-1], int(n_cap),
+                src.data_ptr(), kept.data_ptr(), self._s()
+            ),
+            "nca_b200_prune_refill",
+        )
+        L.check(L.lib().nca_b200_clone(C.byref(st.st), src.data_ptr(), self._s()), "nca_b200_clone")
+        self.launches += 2
+        return src, kept
+
+    # ----------------------------------------------------------- reference-shaped NCHW calls
+    def _nchw_batch(self, x: torch.Tensor, given4: torch.Tensor, clamp: torch.Tensor) -> Batch:
+        B, Cc, H, W = x.shape
+        if Cc != self.channels:
+            raise ValueError(f"state has {Cc} channels, model {self.channels}")
+        given = given4.reshape(B, H, W)
+        cl = clamp.to(self.device, torch.float32).permute(0, 2, 3, 1)  # (B, H, W, c_in)
+        inputs = torch.zeros((B, H, W), dtype=torch.uint8, device=self.device)
+        return self.make_batch(given, cl, inputs, trials=1)
+
+    def step_nchw(self, x, given4, clamp, fire_mask) -> torch.Tensor:
+        """NCA.step on reference-layout tensors (src/nca/model.py:503-525)."""
+        B, Cc, H, W = x.shape
+        b = self._nchw_batch(x, given4, clamp)
+        st = self.new_state(B, H * W)
+        self.load_nchw(st, x)
+        masks = (fire_mask.reshape(1, B, H * W) > 0).to(torch.uint8)
+        self.run(st, b, 1, mode="mask", masks=masks)
+        return self.store_nchw(st).reshape(B, Cc, H, W)
+
+    def apply_clamp_nchw(self, x, given4, clamp) -> torch.Tensor:
+        """NCA.apply_clamp (src/nca/model.py:430-438): a zero-step pass through the state
+        layout re-applies nothing, so the clamp is written by loading x and re-initialising the
+        given cells' input channels."""
+        B, Cc, H, W = x.shape
+        b = self._nchw_batch(x, given4, clamp)
+        st = self.new_state(B, H * W)
+        self.load_nchw(st, x)
+        masks = torch.zeros((1, B, H * W), dtype=torch.uint8, device=self.device)
+        self.run(st, b, 1, mode="mask", masks=masks)  # no cell fires: x kept, given cells clamped
+        return self.store_nchw(st).reshape(B, Cc, H, W)
+
+    def readout_nchw(self, x: torch.Tensor) -> dict[str, torch.Tensor]:
+        B, Cc, H, W = x.shape
+        given = torch.zeros((B, H, W), dtype=torch.uint8, device=self.device)
+        cl = torch.zeros((B, H, W, self.cfg.c_in), dtype=torch.float32, device=self.device)
+        b = self.make_batch(given, cl, given, trials=1)
+        st = self.new_state(B, H * W)
+        self.load_nchw(st, x)
+        r = self.readout(st, b, want_pred=True, want_cell_conf=True)
+        toks = torch.tensor(self.cfg.output_tokens, device=self.device)
+        # pred holds tokens already (no given cells here)
+        return {
+            "decoded": r["pred"].long().reshape(B, H, W),
+            "cell_conf": r["cell_conf"].reshape(B, H, W),
+            "board_conf": r["board_conf"],
+            "tokens": toks,
+        }
+
+
+class B200RolloutBlocks:
+    """Drop-in for nca.engine.inference.UniformRolloutBlocks: runs a block of steps with the
+    fire masks the rollout drew, in one persistent launch."""
+
+    def __init__(self, model, config=None, amp: bool = False):
+        precision = "bf16"
+        if isinstance(config, dict):
+            precision = config.get("precision", "bf16")
+        elif config is not None:
+            precision = getattr(config, "precision", "bf16")
+        self.config = config
+        self.engine = B200Engine(model, precision=precision)
+
+    def __call__(self, x, given4, clamp, fires, noises):
+        if any(n is not None and bool((n != 0).any()) for n in noises):
+            raise ValueError("the b200 backend has no step noise")
+        e = self.engine
+        B, Cc, H, W = x.shape
+        b = e._nchw_batch(x, given4, clamp)
+        st = e.new_state(B, H * W)
+        e.load_nchw(st, x)
+        masks = torch.stack([(f.reshape(B, H * W) > 0) for f in fires]).to(torch.uint8)
+        e.run(st, b, len(fires), mode="mask", masks=masks)
+        return e.store_nchw(st).reshape(B, Cc, H, W)

@@ -1,0 +1,291 @@
+"""CPU oracle of the NCA test-time rollout -- TEST INFRASTRUCTURE, NOT PART OF THE PRODUCT.
+
+A plain numpy (fp32) restatement of the reference's algorithm for the rollout path of
+JorisViaudQuantAI/NCAs, used only by tests/, __graft_entry__.smoke() and bench.py's CPU
+baseline as the checker.  The product (ncas_b200) never imports this module.
+
+Pinning: tests/test_oracle.py checks every function here against golden vectors produced by the
+live reference (tests/golden/make_golden.py imports the reference's own nca package and records
+its outputs), so the restatement is tied to the reference, not to this file's reading of it.
+
+Each function names the reference code it restates (paths relative to the reference root).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+F32 = np.float32
+
+
+# ---------------------------------------------------------------------------- the cell rule
+def perceive(x: np.ndarray, taps: np.ndarray) -> np.ndarray:
+    """KernelPerception with zero padding (src/nca/model.py:140-152, 175-178): x (B, C, H, W)
+    -> z (B, heads*C, H, W), head-major z[:, k*C + c] = sum_n taps[k, n] * x[:, c, shifted n]."""
+    B, C, H, W = x.shape
+    heads = taps.shape[0]
+    t = taps.reshape(heads, 9).astype(F32)
+    xp = np.zeros((B, C, H + 2, W + 2), F32)
+    xp[:, :, 1:-1, 1:-1] = x
+    z = np.zeros((B, heads, C, H, W), F32)
+    for n in range(9):
+        dy, dx = divmod(n, 3)
+        v = xp[:, :, dy : dy + H, dx : dx + W]
+        for k in range(heads):
+            if t[k, n] != 0:
+                z[:, k] += t[k, n] * v
+    return z.reshape(B, heads * C, H, W)
+
+
+def mlp(z: np.ndarray, w1, b1, w2, b2) -> np.ndarray:
+    """MLPUpdate (src/nca/model.py:277-287): per cell dx = W2 relu(W1 z + b1) + b2."""
+    B, P, H, W = z.shape
+    zc = np.ascontiguousarray(z.transpose(0, 2, 3, 1)).reshape(-1, P)
+    h = np.maximum(zc @ w1.reshape(w1.shape[0], -1).T.astype(F32) + b1.astype(F32), F32(0))
+    dx = h @ w2.reshape(w2.shape[0], -1).T.astype(F32) + b2.astype(F32)
+    return np.ascontiguousarray(dx.reshape(B, H, W, -1).transpose(0, 3, 1, 2))
+
+
+def apply_clamp(x, given4, clamp, in_off: int) -> np.ndarray:
+    """NCA.apply_clamp (src/nca/model.py:430-438): input slice of given cells <- clamp."""
+    c_in = clamp.shape[1]
+    out = x.copy()
+    sl = slice(in_off, in_off + c_in)
+    out[:, sl] = np.where(given4, clamp, x[:, sl])
+    return out
+
+
+def step(x, given4, clamp, fire, p: dict) -> np.ndarray:
+    """NCA.step without norm/noise/clock (src/nca/model.py:503-525, residual_update 527-559)."""
+    dx = mlp(perceive(x, p["taps"]), p["w1"], p["b1"], p["w2"], p["b2"])
+    y = (x + fire.astype(F32) * dx).astype(F32)
+    return apply_clamp(y, given4, clamp, p["in_off"])
+
+
+def scores(x, p: dict) -> np.ndarray:
+    """mlp head on the readout slice (src/nca/model.py:596-609): (B, n_out, H, W)."""
+    o = x[:, p["out_off"] : p["out_off"] + p["c_out"]]
+    hw = p["head_w"].reshape(p["head_w"].shape[0], -1).astype(F32)
+    return np.einsum("vc,bchw->bvhw", hw, o).astype(F32) + p["head_b"].astype(F32)[None, :, None, None]
+
+
+def decode(x, p: dict) -> np.ndarray:
+    """Argmax token per cell (src/nca/model.py:615-622); first maximum wins."""
+    return np.asarray(p["out_tokens"])[scores(x, p).argmax(axis=1)]
+
+
+def confidence(x, p: dict) -> np.ndarray:
+    """Max softmax probability per cell, clamped to [0, 1] (src/nca/model.py:624-629)."""
+    s = scores(x, p)
+    m = s.max(axis=1, keepdims=True)
+    e = np.exp(s - m)
+    return np.clip((e / e.sum(axis=1, keepdims=True)).max(axis=1), 0.0, 1.0).astype(F32)
+
+
+def board_confidence(x, p: dict) -> np.ndarray:
+    """Mean cell confidence over all H*W cells (src/nca/model.py:631-633)."""
+    return confidence(x, p).mean(axis=(1, 2), dtype=np.float64).astype(F32)
+
+
+def decode_boards(x, given, inputs, p: dict) -> np.ndarray:
+    """Given cells show their input token (src/nca/rollout.py:74-82)."""
+    return np.where(given, inputs, decode(x, p))
+
+
+def init_state(inputs, given, p: dict, channels: int):
+    """sigma_init = 0 state with the input slice of given cells clamped (src/nca/model.py:
+    384-412): returns (x, given4, clamp)."""
+    B, H, W = inputs.shape
+    clamp = np.ascontiguousarray(p["embed"][inputs].transpose(0, 3, 1, 2)).astype(F32)
+    given4 = given[:, None]
+    x = apply_clamp(np.zeros((B, channels, H, W), F32), given4, clamp, p["in_off"])
+    return x, given4, clamp
+
+
+# ----------------------------------------------------------------------- selection, pruning
+def conf_at_k(metric, conf, alive, ks):
+    """src/nca/rollout.py:317-334 (unweighted)."""
+    N, K = metric.shape
+    out = {}
+    for k in ks:
+        k = min(k, K)
+        c = np.where(alive[:, :k], conf[:, :k], -np.inf)
+        out[k] = float(np.mean(metric[np.arange(N), c.argmax(axis=1)]))
+    return out
+
+
+def best_trial(conf, alive, k):
+    """Per board the first index of the largest alive confidence among trials < k."""
+    return np.where(alive[:, :k], conf[:, :k], -np.inf).argmax(axis=1)
+
+
+def pass_at_k(metric, alive, ks):
+    """src/nca/rollout.py:337-350 (unweighted)."""
+    N, K = metric.shape
+    return {min(k, K): float(np.mean((metric[:, : min(k, K)] & alive[:, : min(k, K)]).any(axis=1)))
+            for k in ks}
+
+
+def niche_capped_pruning(decoded, conf, alive, n_cap, order_fn):
+    """The reference's halving rule, src/nca/pruning.py:22-65: niches by decoded-grid bytes,
+    at most n_cap per niche (stable sort by -conf), survivors round-robin over niches in the
+    order order_fn(n_niches) (the reference draws rng.permutation), until half the alive
+    trials are kept.  decoded (N, K, ...) ints, conf (N, K), alive (N, K) bool."""
+    N, K = conf.shape
+    al = alive.copy()
+    for n in range(N):
+        idx = np.nonzero(al[n])[0]
+        if len(idx) <= 1:
+            continue
+        target = len(idx) // 2
+        niches: dict[bytes, list[int]] = {}
+        for k in idx:
+            niches.setdefault(np.ascontiguousarray(decoded[n, k]).tobytes(), []).append(int(k))
+        capped = [sorted(m, key=lambda k: -conf[n, k])[:n_cap] for m in niches.values()]
+        order = order_fn(len(capped))
+        surv: list[int] = []
+        depth = 0
+        while len(surv) < target:
+            added = False
+            for j in order:
+                if depth < len(capped[j]):
+                    surv.append(capped[j][depth])
+                    added = True
+                    if len(surv) >= target:
+                        break
+            if not added:
+                break
+            depth += 1
+        new = np.zeros(K, dtype=bool)
+        new[surv] = True
+        al[n] = new
+    return al
+
+
+def niche_cap_refill(decoded, conf, n_cap):
+    """Niche-capped pruning with refill (the benchmark's variant of src/nca/pruning.py:22-65):
+    niches by identical decoded grid (pruning.py:39-41), the n_cap most confident members of
+    each kept (stable sort by -conf, pruning.py:43-46), and every dropped slot, in increasing
+    trial order, refilled with a clone of the kept trials ranked by confidence (ties: lower
+    trial first), cycling.  Returns (src (N, K) int: slot k continues from trial src[k],
+    kept (N, K) bool)."""
+    N, K = conf.shape
+    src = np.tile(np.arange(K), (N, 1))
+    kept = np.zeros((N, K), dtype=bool)
+    for n in range(N):
+        niches: dict[bytes, list[int]] = {}
+        for k in range(K):
+            niches.setdefault(np.ascontiguousarray(decoded[n, k]).tobytes(), []).append(k)
+        for members in niches.values():
+            for k in sorted(members, key=lambda k: -conf[n, k])[:n_cap]:
+                kept[n, k] = True
+        ranked = sorted(np.nonzero(kept[n])[0].tolist(), key=lambda k: (-conf[n, k], k))
+        dead = [k for k in range(K) if not kept[n, k]]
+        for i, k in enumerate(dead):
+            src[n, k] = ranked[i % len(ranked)]
+    return src, kept
+
+
+# ------------------------------------------------------------------------------- randomness
+MASK32 = 0xFFFFFFFF
+
+
+def philox4x32_10(ctr, key):
+    """Philox-4x32 with 10 rounds (Salmon et al., SC'11), vectorised over uint64 arrays
+    holding 32-bit lanes.  ctr: 4 arrays, key: 2 ints.  The same published bijection the
+    product kernels use for their counter-based fire masks."""
+    M0, M1, W0, W1 = 0xD2511F53, 0xCD9E8D57, 0x9E3779B9, 0xBB67AE85
+    x, y, z, w = (np.asarray(c, dtype=np.uint64) & MASK32 for c in ctr)
+    k0, k1 = np.uint64(key[0] & MASK32), np.uint64(key[1] & MASK32)
+    for _ in range(10):
+        p0 = np.uint64(M0) * x
+        p1 = np.uint64(M1) * z
+        hi0, lo0 = p0 >> np.uint64(32), p0 & np.uint64(MASK32)
+        hi1, lo1 = p1 >> np.uint64(32), p1 & np.uint64(MASK32)
+        x, y, z, w = (hi1 ^ y ^ k0) & np.uint64(MASK32), lo1, (hi0 ^ w ^ k1) & np.uint64(MASK32), lo0
+        k0 = (k0 + np.uint64(W0)) & np.uint64(MASK32)
+        k1 = (k1 + np.uint64(W1)) & np.uint64(MASK32)
+    return x, y, z, w
+
+
+def philox_uniform(seed: int, inst: np.ndarray, cell: np.ndarray, step: int) -> np.ndarray:
+    """u in [0, 1) (24 bits) for counter (cell, inst_lo, inst_hi, step), key = seed."""
+    inst = np.asarray(inst, dtype=np.int64)
+    cell = np.asarray(cell, dtype=np.int64)
+    inst, cell = np.broadcast_arrays(inst, cell)
+    ctr = (cell.astype(np.uint64), inst.astype(np.uint64) & np.uint64(MASK32),
+           (inst.astype(np.uint64) >> np.uint64(32)), np.full(inst.shape, step & MASK32, np.uint64))
+    o = philox4x32_10(ctr, (seed & MASK32, (seed >> 32) & MASK32))
+    return ((o[0] >> np.uint64(8)).astype(np.float64) * (1.0 / 16777216.0)).astype(F32)
+
+
+def philox_masks(seed: int, inst_offset: int, n_inst: int, hw: int, step: int, p: float):
+    inst = inst_offset + np.arange(n_inst)[:, None]
+    cell = np.arange(hw)[None, :]
+    return philox_uniform(seed, inst, cell, step) < F32(p)
+
+
+def adaptive_prob(conf, scale=0.9, bias=0.1):
+    """The benchmark's continuous adaptive rule p = scale * (1 - conf) + bias, applied to the
+    reference's per-cell confidence (src/nca/model.py:624-629) instead of the reference's
+    threshold rule (src/nca/model.py:587-593)."""
+    return (F32(scale) * (F32(1) - conf) + F32(bias)).astype(F32)
+
+
+# ---------------------------------------------------------------------------------- rollout
+def rollout(p: dict, inputs, given, k: int, depth: int, *, channels: int, masks=None, seed=0,
+            p_fire=0.5, fire="external", inst_offset=0, uniforms=None, adaptive=None,
+            prune_every=0, n_cap=2, targets=None):
+    """Rollout of the benchmark configs (src/nca/rollout.py:86-305 restricted to one pass, no
+    noise/damage): boards repeated k times, `depth` steps, then decoded boards and board
+    confidences.  fire: 'external' (masks (depth, B, H, W) {0,1}), 'philox' (kernel stream),
+    'adaptive_uniform' (uniforms (depth, B, H, W)), 'adaptive_philox'.  prune_every > 0 applies
+    niche_cap_refill every prune_every steps."""
+    inputs_k = np.repeat(inputs, k, axis=0)
+    given_k = np.repeat(given, k, axis=0)
+    x, g4, clamp = init_state(inputs_k, given_k, p, channels)
+    B, _, H, W = x.shape
+    updates = np.zeros(B, dtype=np.int64)
+    for t in range(depth):
+        if fire == "external":
+            fm = masks[t].reshape(B, 1, H, W) != 0
+        elif fire == "philox":
+            fm = philox_masks(seed, inst_offset, B, H * W, t, p_fire).reshape(B, 1, H, W)
+        else:
+            if fire == "adaptive_uniform":
+                u = uniforms[t].reshape(B, 1, H, W)
+            else:
+                u = philox_uniform(seed, inst_offset + np.arange(B)[:, None], np.arange(H * W)[None, :],
+                                   t).reshape(B, 1, H, W)
+            a = adaptive or (0.9, 0.1)
+            fm = u < adaptive_prob(confidence(x, p)[:, None], *a)
+        updates += fm.reshape(B, -1).sum(axis=1)
+        x = step(x, g4, clamp, fm, p)
+        if prune_every and (t + 1) % prune_every == 0 and (t + 1) < depth:
+            dec = decode_boards(x, given_k, inputs_k, p).reshape(-1, k, H * W)
+            conf = board_confidence(x, p).reshape(-1, k)
+            src, _ = niche_cap_refill(dec, conf, n_cap)
+            flat = (src + np.arange(src.shape[0])[:, None] * k).reshape(-1)
+            x = x[flat].copy()
+            updates = updates[flat].copy()
+    dec = decode_boards(x, given_k, inputs_k, p)
+    return {"x": x, "decoded": dec, "conf": board_confidence(x, p), "updates": updates}
+
+
+def params_from_arrays(d: dict, cfg) -> dict:
+    """Oracle parameter dict from the reference-named arrays of a model config."""
+    n_out = len(cfg.output_tokens)
+    return {
+        "taps": np.asarray(d["perceive.weight"], F32).reshape(-1, 9),
+        "w1": np.asarray(d["update.fc1.weight"], F32).reshape(d["update.fc1.weight"].shape[0], -1),
+        "b1": np.asarray(d["update.fc1.bias"], F32),
+        "w2": np.asarray(d["update.fc2.weight"], F32).reshape(d["update.fc2.weight"].shape[0], -1),
+        "b2": np.asarray(d["update.fc2.bias"], F32),
+        "head_w": np.asarray(d["head.weight"], F32).reshape(n_out, -1),
+        "head_b": np.asarray(d["head.bias"], F32),
+        "out_tokens": np.asarray(cfg.output_tokens),
+        "in_off": cfg.in_offset,
+        "out_off": cfg.out_offset,
+        "c_out": cfg.c_out,
+        "embed": np.eye(cfg.vocab_size, cfg.c_in, dtype=F32),
+    }

@@ -1,0 +1,154 @@
+"""Generate tests/golden/golden.npz from the live reference (JorisViaudQuantAI/NCAs).
+
+Run in a container where the reference is importable (it is not on the GPU box):
+
+    PYTHONPATH=/path/to/reference/src python tests/golden/make_golden.py [/path/to/reference]
+
+Every array in the file is produced by the reference's own code: nca.model.NCA (built through
+nca.model.build_model with the benchmark overrides and the benchmark's synthetic weights loaded
+into it), nca.rollout.conf_at_k / pass_at_k, nca.pruning.niche_capped_pruning and the maze /
+sudoku generators of nca.tasks.  The tests compare the oracle and the CUDA kernels against it.
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REPO = Path(__file__).resolve().parents[2]
+REF = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+sys.path.insert(0, str(REF / "src"))
+sys.path.insert(0, str(REPO))
+
+from nca.model import build_model  # noqa: E402  (reference)
+from nca.pruning import niche_capped_pruning  # noqa: E402
+from nca.rollout import conf_at_k, pass_at_k  # noqa: E402
+from nca.tasks.maze import generate_hard_maze, generate_perfect_maze  # noqa: E402
+from nca.tasks.sudoku import sudoku_symmetry  # noqa: E402
+
+from ncas_b200.configs import model_config, synthetic_params  # noqa: E402
+
+torch.set_num_threads(4)
+OUT = Path(__file__).resolve().parent / "golden.npz"
+G: dict[str, np.ndarray] = {}
+
+
+def ref_model(task: str, seed: int):
+    cfg = model_config(task)
+    d = {k: v for k, v in cfg.to_dict().items()}
+    m = build_model(None, **d)
+    with torch.no_grad():
+        for name, v in synthetic_params(cfg, seed).items():
+            m.get_parameter(name).copy_(torch.from_numpy(v))
+    m.eval()
+    return m
+
+
+def second_endpoint_goal(inp: np.ndarray) -> np.ndarray:
+    """D8: the reference's maze-OOD endpoints are both token 3; the one second in row-major
+    order becomes the goal (token 4), as nca.tasks.maze._second_endpoint_as_goal does."""
+    t = inp.astype(np.int64).copy()
+    ends = np.argwhere(t == 3)
+    t[tuple(ends[1])] = 4
+    return t
+
+
+def run_steps(m, inputs, given, K, masks, record=(1,)):
+    inp = torch.from_numpy(np.repeat(inputs, K, 0))
+    gv = torch.from_numpy(np.repeat(given, K, 0))
+    x, g4, clamp = m.init_state(inp, gv)
+    rec = {}
+    with torch.no_grad():
+        for t in range(masks.shape[0]):
+            fm = torch.from_numpy(masks[t].reshape(x.shape[0], 1, *x.shape[2:]).astype(np.float32))
+            x = m.step(x, g4, clamp, fm)
+            if t + 1 in record:
+                rec[t + 1] = x.numpy().copy()
+        dec = torch.where(gv, inp, m.decode(x))
+        return rec, x.numpy(), dec.numpy(), m.confidence(x).numpy(), m.board_confidence(x).numpy()
+
+
+def main() -> None:
+    # ---- maze boards: perfect 19x19 (cfg0 shape), reference generator
+    rng = np.random.default_rng(7)
+    mz = [generate_perfect_maze(19, rng) for _ in range(4)]
+    maze_inputs = np.stack([second_endpoint_goal(i) for i, _ in mz])
+    maze_targets = np.stack([second_endpoint_goal(t) for _, t in mz])
+    G["maze_inputs"], G["maze_targets"] = maze_inputs.astype(np.uint8), maze_targets.astype(np.uint8)
+    rng = np.random.default_rng(8)
+    hard = [generate_hard_maze(30, rng, min_path_len=60, extra_openings=0.10) for _ in range(2)]
+    G["hard_inputs"] = np.stack([h[0] for h in hard]).astype(np.uint8)
+
+    # ---- maze rollout: 4 boards, K=1, 64 steps, seeded external masks
+    m = ref_model("maze", 0)
+    maze_given = maze_inputs != 0
+    masks = (np.random.default_rng(11).random((64, 4, 19 * 19)) < 0.5).astype(np.uint8)
+    rec, x64, dec, cconf, bconf = run_steps(m, maze_inputs, maze_given, 1, masks, record=(1,))
+    G.update(maze_masks=masks, maze_x1=rec[1], maze_x64=x64, maze_dec64=dec.astype(np.uint8),
+             maze_cconf64=cconf, maze_bconf64=bconf)
+
+    # ---- sudoku: 4 boards, K=2, 64 steps
+    rng = np.random.default_rng(21)
+    syms = [sudoku_symmetry(rng) for _ in range(3)]
+    G["sym_rows"] = np.stack([s[0] for s in syms])
+    G["sym_cols"] = np.stack([s[1] for s in syms])
+    G["sym_tr"] = np.array([s[2] for s in syms])
+    G["sym_digits"] = np.stack([s[3] for s in syms])
+    from ncas_b200.tasks import sudoku_boards
+
+    sb = sudoku_boards(4, seed=5)
+    G["sudoku_inputs"], G["sudoku_given"] = sb.inputs.astype(np.uint8), sb.given
+    G["sudoku_targets"] = sb.targets.astype(np.uint8)
+    m = ref_model("sudoku", 0)
+    masks = (np.random.default_rng(12).random((64, 8, 81)) < 0.5).astype(np.uint8)
+    rec, x64, dec, cconf, bconf = run_steps(m, sb.inputs, sb.given, 2, masks, record=(1,))
+    G.update(sudoku_masks=masks, sudoku_x1=rec[1], sudoku_x64=x64, sudoku_dec64=dec.astype(np.uint8),
+             sudoku_cconf64=cconf, sudoku_bconf64=bconf)
+
+    # ---- adaptive (continuous rule on the reference's confidence), 16 steps
+    inp = torch.from_numpy(np.repeat(sb.inputs, 2, 0))
+    gv = torch.from_numpy(np.repeat(sb.given, 2, 0))
+    x, g4, clamp = m.init_state(inp, gv)
+    u = np.random.default_rng(13).random((16, 8, 81)).astype(np.float32)
+    fired = np.zeros(8, np.int64)
+    with torch.no_grad():
+        for t in range(16):
+            conf = m.confidence(x)[:, None]
+            prob = 0.9 * (1 - conf) + 0.1
+            fm = (torch.from_numpy(u[t].reshape(8, 1, 9, 9)) < prob).float()
+            fired += fm.reshape(8, -1).sum(1).long().numpy()
+            x = m.step(x, g4, clamp, fm)
+    G.update(adapt_u=u, adapt_x16=x.numpy(), adapt_fired=fired,
+             adapt_dec16=torch.where(gv, inp, m.decode(x)).numpy().astype(np.uint8))
+
+    # ---- conf@K / pass@K on random inputs
+    r = np.random.default_rng(31)
+    metric = r.random((20, 8)) < 0.4
+    conf = r.random((20, 8)).astype(np.float32)
+    conf[3, 2] = conf[3, 5]  # a tie: the first index must win
+    alive = r.random((20, 8)) < 0.8
+    ks = [1, 2, 4, 8]
+    ck, pk = conf_at_k(metric, conf, alive, ks), pass_at_k(metric, alive, ks)
+    G.update(sel_metric=metric, sel_conf=conf, sel_alive=alive,
+             sel_confk=np.array([ck[k] for k in ks]), sel_passk=np.array([pk[k] for k in ks]))
+
+    # ---- niche-capped pruning (reference halving rule) with its rng
+    r = np.random.default_rng(41)
+    dec = r.integers(0, 3, size=(6, 8, 2, 2))
+    dec[:, :4] = dec[:, :1]  # duplicates: trials 0..3 share a niche
+    pconf = r.random((6, 8)).astype(np.float32)
+    palive = np.ones((6, 8), dtype=bool)
+    palive[5, 6:] = False
+    new = niche_capped_pruning(torch.from_numpy(dec), torch.from_numpy(pconf), torch.from_numpy(palive),
+                               2, np.random.default_rng(42))
+    G.update(prune_dec=dec, prune_conf=pconf, prune_alive=palive, prune_new=new.numpy())
+
+    np.savez_compressed(OUT, **G)
+    print(f"wrote {OUT} ({OUT.stat().st_size / 1e3:.0f} kB, {len(G)} arrays)")
+
+
+if __name__ == "__main__":
+    main()

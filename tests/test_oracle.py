@@ -1,0 +1,112 @@
+"""The CPU oracle against golden vectors recorded from the live reference (no GPU)."""
+
+import numpy as np
+import pytest
+
+import oracle.nca_oracle as O
+from ncas_b200.configs import bf16_round, model_config, synthetic_params
+
+
+def params(task):
+    cfg = model_config(task)
+    return O.params_from_arrays(synthetic_params(cfg, 0), cfg), cfg
+
+
+def test_synthetic_weights_are_bf16_values():
+    cfg = model_config("sudoku")
+    d = synthetic_params(cfg, 0)
+    w = d["update.fc1.weight"]
+    assert np.array_equal(bf16_round(w), w)
+    assert 0.015 < float(w.std()) < 0.025
+
+
+@pytest.mark.parametrize("task", ["maze", "sudoku"])
+def test_one_step_matches_reference(golden, task):
+    p, cfg = params(task)
+    inputs = golden[f"{task}_inputs"].astype(np.int64)
+    given = golden["sudoku_given"] if task == "sudoku" else inputs != 0
+    K = 2 if task == "sudoku" else 1
+    x, g4, clamp = O.init_state(np.repeat(inputs, K, 0), np.repeat(given, K, 0), p, cfg.channels)
+    m = golden[f"{task}_masks"][0].reshape(x.shape[0], 1, *x.shape[2:])
+    x1 = O.step(x, g4, clamp, m, p)
+    np.testing.assert_allclose(x1, golden[f"{task}_x1"], atol=1e-6, rtol=0)
+
+
+@pytest.mark.parametrize("task", ["maze", "sudoku"])
+def test_64_step_rollout_matches_reference(golden, task):
+    p, cfg = params(task)
+    inputs = golden[f"{task}_inputs"].astype(np.int64)
+    given = golden["sudoku_given"] if task == "sudoku" else inputs != 0
+    K = 2 if task == "sudoku" else 1
+    out = O.rollout(p, inputs, given, K, 64, channels=cfg.channels, masks=golden[f"{task}_masks"])
+    np.testing.assert_allclose(out["x"], golden[f"{task}_x64"], atol=2e-5, rtol=0)
+    assert np.array_equal(out["decoded"], golden[f"{task}_dec64"])
+    np.testing.assert_allclose(O.confidence(out["x"], p), golden[f"{task}_cconf64"], atol=1e-5)
+    np.testing.assert_allclose(out["conf"], golden[f"{task}_bconf64"], atol=1e-6)
+
+
+def test_adaptive_rule_matches_reference(golden):
+    p, cfg = params("sudoku")
+    u = golden["adapt_u"]
+    out = O.rollout(p, golden["sudoku_inputs"].astype(np.int64), golden["sudoku_given"], 2, 16,
+                    channels=64, fire="adaptive_uniform", uniforms=u)
+    np.testing.assert_allclose(out["x"], golden["adapt_x16"], atol=2e-5, rtol=0)
+    assert np.array_equal(out["updates"], golden["adapt_fired"])
+    assert np.array_equal(out["decoded"], golden["adapt_dec16"])
+
+
+def test_zero_fire_mask_is_identity(golden):
+    """src/nca/model.py step with an all-zero mask leaves the clamped state unchanged
+    (tests/test_model.py:71-79 of the reference)."""
+    p, cfg = params("maze")
+    inputs = golden["maze_inputs"].astype(np.int64)
+    x, g4, clamp = O.init_state(inputs, inputs != 0, p, 32)
+    x = x + np.random.default_rng(0).standard_normal(x.shape).astype(np.float32) * 0.1
+    x = O.apply_clamp(x, g4, clamp, 0)
+    assert np.array_equal(O.step(x, g4, clamp, np.zeros((4, 1, 19, 19)), p), x)
+
+
+def test_given_cells_stay_clamped(golden):
+    p, cfg = params("sudoku")
+    out = O.rollout(p, golden["sudoku_inputs"].astype(np.int64), golden["sudoku_given"], 2, 8,
+                    channels=64, masks=np.ones((8, 8, 81), np.uint8))
+    x = out["x"]
+    g = np.repeat(golden["sudoku_given"], 2, 0)
+    toks = np.repeat(golden["sudoku_inputs"], 2, 0).astype(np.int64)
+    emb = p["embed"][toks]  # (B, 9, 9, 10)
+    assert np.array_equal(x[:, :10].transpose(0, 2, 3, 1)[g], emb[g])
+
+
+def test_fixed_perception_equals_block_diagonal_conv():
+    """KernelPerception = dense conv with block-diagonal weights (tests/test_model.py:34-49)."""
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((2, 5, 7, 7)).astype(np.float32)
+    taps = rng.standard_normal((3, 9)).astype(np.float32)
+    z = O.perceive(x, taps)
+    xp = np.pad(x, ((0, 0), (0, 0), (1, 1), (1, 1)))
+    for k in range(3):
+        for c in range(5):
+            ref = sum(taps[k, n] * xp[:, c, n // 3 : n // 3 + 7, n % 3 : n % 3 + 7] for n in range(9))
+            np.testing.assert_allclose(z[:, k * 5 + c], ref, atol=1e-5)
+
+
+# Known-answer vectors of Philox4x32-10 (Salmon et al., SC'11; the Random123 distribution's
+# kat_vectors file): counter, key -> output.
+PHILOX_KAT = [
+    ((0, 0, 0, 0), (0, 0), (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)),
+    ((0xFFFFFFFF,) * 4, (0xFFFFFFFF, 0xFFFFFFFF), (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)),
+    ((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0),
+     (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1)),
+]
+
+
+@pytest.mark.parametrize("ctr,key,want", PHILOX_KAT)
+def test_philox_known_answers(ctr, key, want):
+    out = O.philox4x32_10([np.array([c], np.uint64) for c in ctr], key)
+    assert tuple(int(o[0]) for o in out) == want
+
+
+def test_philox_uniform_range_and_rate():
+    u = O.philox_uniform(123, np.arange(64)[:, None], np.arange(900)[None, :], 7)
+    assert u.dtype == np.float32 and u.min() >= 0 and u.max() < 1
+    assert abs(float((u < 0.5).mean()) - 0.5) < 0.01

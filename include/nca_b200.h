@@ -175,7 +175,8 @@ int32_t nca_b200_prune_refill(const uint8_t* pred, const float* board_conf, int3
                               int32_t trials, int32_t hw, int32_t n_cap, int32_t* src,
                               uint8_t* kept, void* stream);
 /* Copies the state of instance src[i] into instance i wherever src[i] != i (the batch gather
- * x[sel] of src/nca/rollout.py:270-274, without compaction). */
+ * x[sel] of src/nca/rollout.py:270-274, without compaction).  In place: every source must map to
+ * itself (src[src[i]] == src[i]), as the maps written by nca_b200_prune_refill do. */
 int32_t nca_b200_clone(NcaState* st, const int32_t* src, void* stream);
 
 /* ---- control words ------------------------------------------------------------------------ */

@@ -104,7 +104,7 @@ def test_readout_matches_reference(golden, precision):
     b = eng.batch_from_boards(inputs, given, K)
     st = eng.new_state(8, 81)
     eng.load_nchw(st, torch.from_numpy(golden["sudoku_x64"]))
-    tg = torch.from_numpy(np.repeat(golden["sudoku_targets"], K, 0))
+    tg = torch.from_numpy(golden["sudoku_targets"])  # per board row, shared by its K trials
     r = eng.readout(st, b, targets=tg, want_cell_conf=True)
     eng.check()
     assert np.array_equal(r["pred"].reshape(8, 9, 9).cpu().numpy(), golden["sudoku_dec64"])
@@ -213,7 +213,7 @@ def test_clone_copies_states():
     boards = maze_boards(2, 19, seed=2)
     masks = (np.random.default_rng(6).random((3, 8, 361)) < 0.5).astype(np.uint8)
     eng, st, b, x = run_kernel("maze", "bf16", boards.inputs, boards.given, 4, masks)
-    src = torch.tensor([0, 0, 2, 1, 4, 7, 6, 7], dtype=torch.int32, device=DEV)
+    src = torch.tensor([0, 0, 2, 2, 4, 7, 6, 7], dtype=torch.int32, device=DEV)  # sources map to themselves
     L.check(L.lib().nca_b200_clone(C.byref(st.st), src.data_ptr(), eng._s()), "clone")
     y = eng.store_nchw(st).reshape(8, 32, 19, 19).cpu().numpy()
     assert np.array_equal(y, x[src.cpu().numpy()])

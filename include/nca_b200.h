@@ -41,7 +41,8 @@ typedef enum NcaStatus {
   NCA_ERR_CUDA = 3,         /* a CUDA runtime call failed */
   NCA_ERR_TIMEOUT = 4,      /* a bounded wait inside a kernel ran out (see ctrl words) */
   NCA_ERR_DEVICE = 5,       /* no sm_100 device, or the kernel image does not load */
-  NCA_ERR_KERNEL = 6        /* a kernel reported an internal check failure (see ctrl words) */
+  NCA_ERR_KERNEL = 6,       /* a kernel reported an internal check failure (see ctrl words) */
+  NCA_ERR_SCRATCH = 7       /* request larger than the static scratch of nca_b200_run_steps_static */
 } NcaStatus;
 
 typedef enum NcaPrecision {
@@ -186,6 +187,35 @@ int32_t nca_b200_ctrl_status(int32_t* ctrl, int32_t* detail, void* stream);
 /* Self-test of the bounded waits: launches a kernel that waits for a flag nothing sets, with
  * the given timeout; returns NCA_ERR_TIMEOUT (the expected result) when the wait gave up. */
 int32_t nca_b200_selftest_timeout(int32_t* ctrl, int32_t timeout_ms, void* stream);
+
+/* ---- stepping without any device allocation ---------------------------------------------- */
+/* Size of the library's file-scope device array used by nca_b200_run_steps_static: 16 MiB.  Every
+ * GPU that loads the library holds it until the process exits. */
+#define NCA_B200_STATIC_SCRATCH_BYTES (16u << 20)
+
+/* For callers that cannot allocate device memory: code running inside a CUDA graph being built,
+ * a host framework whose allocator owns all device memory and hands out only the caller's
+ * tensors, or an embedded runtime with a fixed memory budget.  It runs the same n_steps as
+ * nca_b200_run_steps, but the kernel's scratch (the ping-pong state workspace and the four
+ * control words) lives in a static 16 MiB device array inside the library instead of buffers
+ * the caller allocates; the caller passes only inputs and outputs: the fp32 NCHW state before
+ * (x_in) and after (x_out) the steps, both n_inst x channels x H x W.
+ *  - Limit: nca_b200_state_bytes(n_inst, H*W, channels, state_precision) + 256 bytes must fit in
+ *    NCA_B200_STATIC_SCRATCH_BYTES, else NCA_ERR_SCRATCH (e.g. 21,000 Sudoku cells at C = 64 or one
+ *    201 x 201 maze at C = 32 in bf16 mode).
+ *  - It calls no allocator.  Its first call on a device looks up the device address of the array
+ *    (cudaGetSymbolAddress with that device current); make that first call before any stream
+ *    capture on the device.
+ *  - All calls share the one array, which keeps the last call's contents; the call clears the
+ *    control words and rewrites the state workspace before use.  Calls that overlap on the GPU
+ *    (other streams, other host threads) race on the array: serialise them.
+ *  - It waits for its own work: the stream is synchronised before it returns, so that a kernel
+ *    timeout comes back as NCA_ERR_TIMEOUT.
+ * There is no counterpart in the reference: it is an addition of this library. */
+int32_t nca_b200_run_steps_static(const NcaModelDesc* m, const NcaBatchDesc* b,
+                                  int32_t state_precision, const float* x_in, float* x_out,
+                                  int32_t n_steps, const NcaFireDesc* fire, int32_t timeout_ms,
+                                  void* stream);
 
 #ifdef __cplusplus
 }

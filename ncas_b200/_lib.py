@@ -25,6 +25,7 @@ STATUS_NAMES = {
     4: "NCA_ERR_TIMEOUT",
     5: "NCA_ERR_DEVICE",
     6: "NCA_ERR_KERNEL",
+    7: "NCA_ERR_SCRATCH",
 }
 PREC_BF16, PREC_SPLIT = 0, 1
 FIRE_MASK, FIRE_PHILOX, FIRE_ADAPTIVE_PHILOX, FIRE_ADAPTIVE_UNIFORM = 0, 1, 2, 3
@@ -142,6 +143,10 @@ SIGNATURES = {
     "nca_b200_clone": (_I, [C.POINTER(NcaState), _P, _P]),
     "nca_b200_ctrl_status": (_I, [_P, C.POINTER(_I), _P]),
     "nca_b200_selftest_timeout": (_I, [_P, _I, _P]),
+    "nca_b200_run_steps_static": (
+        _I,
+        [C.POINTER(NcaModelDesc), C.POINTER(NcaBatchDesc), _I, _P, _P, _I, C.POINTER(NcaFireDesc), _I, _P],
+    ),
 }
 
 _lib: C.CDLL | None = None

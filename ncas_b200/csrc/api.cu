@@ -434,6 +434,7 @@ const char* nca_b200_status_string(int32_t s) {
     case NCA_ERR_TIMEOUT: return "a bounded wait inside a kernel ran out";
     case NCA_ERR_DEVICE: return "no usable sm_100 device";
     case NCA_ERR_KERNEL: return "kernel-side check failed";
+    case NCA_ERR_SCRATCH: return "request larger than the static scratch of nca_b200_run_steps_static";
     default: return "unknown status";
   }
 }
@@ -656,3 +657,58 @@ int32_t nca_b200_selftest_timeout(int32_t* ctrl, int32_t timeout_ms, void* strea
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------
+// Stepping without device allocation: the scratch of nca_b200_run_steps lives in this array.
+namespace {
+
+__device__ __align__(256) uint8_t g_static_scratch[NCA_B200_STATIC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+void* g_static_scratch_addr[kMaxDevices] = {};
+
+// Device address of g_static_scratch on the current device (looked up once per device).
+int32_t static_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return NCA_ERR_DEVICE;
+  if (g_static_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || p == nullptr)
+      return NCA_ERR_CUDA;
+    g_static_scratch_addr[dev] = p;
+  }
+  *out = g_static_scratch_addr[dev];
+  return NCA_OK;
+}
+
+}  // namespace
+
+extern "C" int32_t nca_b200_run_steps_static(const NcaModelDesc* m, const NcaBatchDesc* b,
+                                             int32_t state_precision, const float* x_in,
+                                             float* x_out, int32_t n_steps,
+                                             const NcaFireDesc* fire, int32_t timeout_ms,
+                                             void* stream) {
+  if (!model_ok(m) || !batch_ok(b) || !fire || !x_in || !x_out || n_steps < 0) return NCA_ERR_INVALID;
+  size_t need = 0;
+  int32_t s = nca_b200_state_bytes(b->n_inst, b->height * b->width, m->channels, state_precision, &need);
+  if (s != NCA_OK) return s;
+  constexpr size_t kCtrlBytes = 256;  // control words, padded to keep the state 256-B aligned
+  if (need + kCtrlBytes > (size_t)NCA_B200_STATIC_SCRATCH_BYTES) return NCA_ERR_SCRATCH;
+  void* base = nullptr;
+  s = static_scratch(&base);
+  if (s != NCA_OK) return s;
+  int32_t* ctrl = reinterpret_cast<int32_t*>(base);
+  cudaStream_t st_ = as_stream(stream);
+  if (cudaMemsetAsync(ctrl, 0, 4 * sizeof(int32_t), st_) != cudaSuccess) return NCA_ERR_CUDA;
+  NcaState st;
+  s = nca_b200_state_bind(&st, reinterpret_cast<uint8_t*>(base) + kCtrlBytes, need, b->n_inst,
+                          b->height * b->width, m->channels, state_precision);
+  if (s != NCA_OK) return s;
+  s = nca_b200_state_load_nchw(&st, x_in, stream);
+  if (s != NCA_OK) return s;
+  s = nca_b200_run_steps(m, b, &st, n_steps, fire, ctrl, timeout_ms, stream);
+  if (s != NCA_OK) return s;
+  s = nca_b200_state_store_nchw(&st, x_out, stream);
+  if (s != NCA_OK) return s;
+  return nca_b200_ctrl_status(ctrl, nullptr, stream);
+}

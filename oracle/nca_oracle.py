@@ -19,30 +19,48 @@ F32 = np.float32
 
 
 # ---------------------------------------------------------------------------- the cell rule
-def perceive(x: np.ndarray, taps: np.ndarray) -> np.ndarray:
-    """KernelPerception with zero padding (src/nca/model.py:140-152, 175-178): x (B, C, H, W)
-    -> z (B, heads*C, H, W), head-major z[:, k*C + c] = sum_n taps[k, n] * x[:, c, shifted n]."""
-    B, C, H, W = x.shape
+def perceive_nhwc(x: np.ndarray, taps: np.ndarray) -> np.ndarray:
+    """KernelPerception with zero padding on a channels-last state: x (B, H, W, C) ->
+    z (B, H, W, heads*C), head-major z[..., k*C + c] = sum_n taps[k, n] * x[shifted n, c]
+    (src/nca/model.py:140-152, 175-178; taps summed in row-major order n = 0..8)."""
+    B, H, W, C = x.shape
     heads = taps.shape[0]
     t = taps.reshape(heads, 9).astype(F32)
-    xp = np.zeros((B, C, H + 2, W + 2), F32)
-    xp[:, :, 1:-1, 1:-1] = x
-    z = np.zeros((B, heads, C, H, W), F32)
+    xp = np.zeros((B, H + 2, W + 2, C), F32)
+    xp[:, 1:-1, 1:-1] = x
+    z = np.zeros((B, H, W, heads, C), F32)
+    tmp = np.empty((B, H, W, C), F32)
     for n in range(9):
         dy, dx = divmod(n, 3)
-        v = xp[:, :, dy : dy + H, dx : dx + W]
+        v = xp[:, dy : dy + H, dx : dx + W]
         for k in range(heads):
             if t[k, n] != 0:
-                z[:, k] += t[k, n] * v
-    return z.reshape(B, heads * C, H, W)
+                np.multiply(v, t[k, n], out=tmp)
+                np.add(z[..., k, :], tmp, out=z[..., k, :])
+    return z.reshape(B, H, W, heads * C)
+
+
+def perceive(x: np.ndarray, taps: np.ndarray) -> np.ndarray:
+    """perceive_nhwc on the reference's (B, C, H, W) layout: z (B, heads*C, H, W)."""
+    z = perceive_nhwc(np.ascontiguousarray(x.transpose(0, 2, 3, 1)), taps)
+    return np.ascontiguousarray(z.transpose(0, 3, 1, 2))
+
+
+def mlp_rows(z: np.ndarray, w1, b1, w2, b2) -> np.ndarray:
+    """MLPUpdate (src/nca/model.py:277-287) on rows of cells: z (M, P) -> dx (M, C) with
+    dx = W2 relu(W1 z + b1) + b2 in fp32."""
+    h = z @ w1.reshape(w1.shape[0], -1).T.astype(F32)
+    np.add(h, b1.astype(F32), out=h)
+    np.maximum(h, F32(0), out=h)
+    dx = h @ w2.reshape(w2.shape[0], -1).T.astype(F32)
+    np.add(dx, b2.astype(F32), out=dx)
+    return dx
 
 
 def mlp(z: np.ndarray, w1, b1, w2, b2) -> np.ndarray:
-    """MLPUpdate (src/nca/model.py:277-287): per cell dx = W2 relu(W1 z + b1) + b2."""
+    """mlp_rows on the (B, P, H, W) layout."""
     B, P, H, W = z.shape
-    zc = np.ascontiguousarray(z.transpose(0, 2, 3, 1)).reshape(-1, P)
-    h = np.maximum(zc @ w1.reshape(w1.shape[0], -1).T.astype(F32) + b1.astype(F32), F32(0))
-    dx = h @ w2.reshape(w2.shape[0], -1).T.astype(F32) + b2.astype(F32)
+    dx = mlp_rows(np.ascontiguousarray(z.transpose(0, 2, 3, 1)).reshape(-1, P), w1, b1, w2, b2)
     return np.ascontiguousarray(dx.reshape(B, H, W, -1).transpose(0, 3, 1, 2))
 
 
@@ -55,11 +73,26 @@ def apply_clamp(x, given4, clamp, in_off: int) -> np.ndarray:
     return out
 
 
+def step_nhwc(x, given, clamp_nhwc, fire, p: dict) -> np.ndarray:
+    """NCA.step without norm/noise/clock (src/nca/model.py:503-525, residual_update 527-559)
+    on channels-last arrays: x (B, H, W, C), given (B, H, W) bool, clamp (B, H, W, c_in),
+    fire (B, H, W) {0, 1}.  x' = x + fire * dx, then the clamp."""
+    B, H, W, C = x.shape
+    z = perceive_nhwc(x, p["taps"])
+    dx = mlp_rows(z.reshape(B * H * W, -1), p["w1"], p["b1"], p["w2"], p["b2"]).reshape(B, H, W, C)
+    np.multiply(dx, fire.reshape(B, H, W, 1).astype(F32), out=dx)
+    np.add(dx, x, out=dx)
+    sl = slice(p["in_off"], p["in_off"] + clamp_nhwc.shape[-1])
+    dx[..., sl] = np.where(given[..., None], clamp_nhwc, dx[..., sl])
+    return dx
+
+
 def step(x, given4, clamp, fire, p: dict) -> np.ndarray:
-    """NCA.step without norm/noise/clock (src/nca/model.py:503-525, residual_update 527-559)."""
-    dx = mlp(perceive(x, p["taps"]), p["w1"], p["b1"], p["w2"], p["b2"])
-    y = (x + fire.astype(F32) * dx).astype(F32)
-    return apply_clamp(y, given4, clamp, p["in_off"])
+    """step_nhwc on the reference's layouts: x (B, C, H, W), given4 (B, 1, H, W), clamp
+    (B, c_in, H, W), fire (B, 1, H, W)."""
+    y = step_nhwc(np.ascontiguousarray(x.transpose(0, 2, 3, 1)), given4[:, 0],
+                  np.ascontiguousarray(clamp.transpose(0, 2, 3, 1)), np.asarray(fire)[:, 0], p)
+    return np.ascontiguousarray(y.transpose(0, 3, 1, 2))
 
 
 def scores(x, p: dict) -> np.ndarray:
@@ -245,29 +278,34 @@ def rollout(p: dict, inputs, given, k: int, depth: int, *, channels: int, masks=
     given_k = np.repeat(given, k, axis=0)
     x, g4, clamp = init_state(inputs_k, given_k, p, channels)
     B, _, H, W = x.shape
+    xs = np.ascontiguousarray(x.transpose(0, 2, 3, 1))
+    clamp_s = np.ascontiguousarray(clamp.transpose(0, 2, 3, 1))
+    nchw = lambda a: np.ascontiguousarray(a.transpose(0, 3, 1, 2))  # noqa: E731
     updates = np.zeros(B, dtype=np.int64)
     for t in range(depth):
         if fire == "external":
-            fm = masks[t].reshape(B, 1, H, W) != 0
+            fm = masks[t].reshape(B, H, W) != 0
         elif fire == "philox":
-            fm = philox_masks(seed, inst_offset, B, H * W, t, p_fire).reshape(B, 1, H, W)
+            fm = philox_masks(seed, inst_offset, B, H * W, t, p_fire).reshape(B, H, W)
         else:
             if fire == "adaptive_uniform":
-                u = uniforms[t].reshape(B, 1, H, W)
+                u = uniforms[t].reshape(B, H, W)
             else:
                 u = philox_uniform(seed, inst_offset + np.arange(B)[:, None], np.arange(H * W)[None, :],
-                                   t).reshape(B, 1, H, W)
+                                   t).reshape(B, H, W)
             a = adaptive or (0.9, 0.1)
-            fm = u < adaptive_prob(confidence(x, p)[:, None], *a)
+            fm = u < adaptive_prob(confidence(nchw(xs), p), *a)
         updates += fm.reshape(B, -1).sum(axis=1)
-        x = step(x, g4, clamp, fm, p)
+        xs = step_nhwc(xs, given_k, clamp_s, fm, p)
         if prune_every and (t + 1) % prune_every == 0 and (t + 1) < depth:
+            x = nchw(xs)
             dec = decode_boards(x, given_k, inputs_k, p).reshape(-1, k, H * W)
             conf = board_confidence(x, p).reshape(-1, k)
             src, _ = niche_cap_refill(dec, conf, n_cap)
             flat = (src + np.arange(src.shape[0])[:, None] * k).reshape(-1)
-            x = x[flat].copy()
+            xs = xs[flat].copy()
             updates = updates[flat].copy()
+    x = nchw(xs)
     dec = decode_boards(x, given_k, inputs_k, p)
     return {"x": x, "decoded": dec, "conf": board_confidence(x, p), "updates": updates}
 

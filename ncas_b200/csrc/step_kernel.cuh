@@ -51,12 +51,18 @@ struct StepCfg {
   static constexpr int NZ = (2 * SLOT_COLS + HD <= 512) ? 2 : 1;
   static constexpr int ACC_COL = NZ * SLOT_COLS;
   static constexpr int TMEM_COLS = pow2ceil(ACC_COL + HD);
+  // bf16 mode keeps h in the accumulator region (each epilogue thread overwrites the columns it
+  // has read), so a z slot is free as soon as GEMM1 is done; acc2 then sits in columns
+  // [HD/4, HD/2) of the region.  Split mode writes h (hi and lo) over the consumed z slot.
+  static constexpr bool H_IN_ACC = !SPLIT_;
+  static constexpr int ACC2_COL = ACC_COL + (H_IN_ACC ? HD / 4 : 0);
   static constexpr int W1_BYTES = HD * P * 2;
   static constexpr int W2_BYTES = C * HD * 2;
   static_assert(ACC_COL + HD <= 512, "tensor memory budget");
   static_assert(C % 16 == 0 && HD % 32 == 0 && HD <= 256 && P % 64 == 0 && HD % 64 == 0,
                 "shape constraints of the UMMA tiles");
   static_assert(NCH % 2 == 0, "stencil channel halves");
+  static_assert(!H_IN_ACC || C <= HD / 4, "acc2 must fit next to h in the accumulator region");
 };
 
 struct StepArgs {
@@ -115,6 +121,8 @@ enum BarId {
   BAR_ACC_EMPTY = 11,
   BAR_WEIGHTS = 12,
   BAR_DRAIN = 13,
+  BAR_ACC_FULL_B = 14,  // second half of GEMM1 (hidden units HD/2 .. HD)
+  BAR_H_FULL_B = 15,    // second half of the hidden epilogue
 };
 
 // Failure sites reported in ctrl[1].
@@ -123,14 +131,9 @@ enum Where {
   W_ST_WINFULL, W_ST_ZEMPTY, W_E1_ACC, W_E2_ACC2, W_DRAIN
 };
 
-// Bank swizzle of a window stage: 16-byte chunk `ch` of window cell `wc` lives at position
-// ch ^ swz(wc), so that 8 consecutive cells read by 8 lanes hit 8 distinct bank groups.
-template <int NCH>
-__device__ __forceinline__ int win_swz(int wc) {
-  if constexpr (NCH >= 8) return wc & 7;
-  else if constexpr (NCH == 4) return (wc >> 1) & 3;
-  else return (wc >> 2) & 1;
-}
+// A window stage is laid out [chunk][window cell][16 B]: lanes that read the same chunk of
+// consecutive cells touch consecutive 16-byte words (no bank conflicts), and every chunk of the
+// window is a copy of contiguous rows of the tiled state layout (a few 1-D bulk copies).
 
 // Warp-converged bounded wait (all 32 lanes call it).
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const FailState& fs,
@@ -211,13 +214,15 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
   if (threadIdx.x == 0) {
     *abort_flag = 0;
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&bars[BAR_WIN_FULL + s], 32);
+      mbar_init(&bars[BAR_WIN_FULL + s], 1);
       mbar_init(&bars[BAR_WIN_EMPTY + s], 8);
       mbar_init(&bars[BAR_Z_FULL + s], 8);
       mbar_init(&bars[BAR_Z_EMPTY + s], 1);
     }
     mbar_init(&bars[BAR_ACC_FULL], 1);
-    mbar_init(&bars[BAR_H_FULL], 8);
+    mbar_init(&bars[BAR_ACC_FULL_B], 1);
+    mbar_init(&bars[BAR_H_FULL], 4);
+    mbar_init(&bars[BAR_H_FULL_B], 4);
     mbar_init(&bars[BAR_ACC2_FULL], 1);
     mbar_init(&bars[BAR_ACC_EMPTY], 8);
     mbar_init(&bars[BAR_WEIGHTS], 1);
@@ -256,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
       }
       const uint32_t w1 = smem_u32(smem + L.w1);
       const uint32_t w2 = smem_u32(smem + L.w2);
-      const uint32_t id1 = idesc_bf16_f32(kTileM, Cfg::HD);
+      const uint32_t id1 = idesc_bf16_f32(kTileM, Cfg::HD / 2);
       const uint32_t id2 = idesc_bf16_f32(kTileM, Cfg::C);
       long long it = 0;
       for (int s = 0; ok && s < A.n_steps; ++s) {
@@ -267,27 +272,49 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           if (!mbar_wait(&bars[BAR_Z_FULL + slot], u & 1, fs, W_MMA_ZFULL)) { ok = false; break; }
           if (!mbar_wait(&bars[BAR_ACC_EMPTY], ((uint32_t)it & 1) ^ 1, fs, W_MMA_ACCEMPTY)) { ok = false; break; }
           tc_fence_after();
+          // GEMM1 in two N halves (hidden units [0, HD/2) then [HD/2, HD)).  In bf16 mode each half
+          // is committed on its own, so that the hidden epilogue of the first half overlaps the
+          // second half, and the z slot is released right after GEMM1.
 #pragma unroll 1
-          for (int kk = 0; kk < Cfg::P / 16; ++kk) {
-            const uint64_t bd = umma_desc_sw128(w1 + (kk >> 2) * (Cfg::HD * 128) + (kk & 3) * 32);
-#pragma unroll
-            for (int part = 0; part < Cfg::ZPARTS; ++part)
-              umma_bf16_ts(tmem + Cfg::ACC_COL, zcol + part * (Cfg::P / 2) + kk * 8, bd, id1,
-                           (kk | part) != 0);
-          }
-          umma_commit(&bars[BAR_ACC_FULL]);
-          if (!mbar_wait(&bars[BAR_H_FULL], (uint32_t)it & 1, fs, W_MMA_HFULL)) { ok = false; break; }
-          tc_fence_after();
+          for (int nh = 0; nh < 2; ++nh) {
 #pragma unroll 1
-          for (int kk = 0; kk < Cfg::HD / 16; ++kk) {
-            const uint64_t bd = umma_desc_sw128(w2 + (kk >> 2) * (Cfg::C * 128) + (kk & 3) * 32);
+            for (int kk = 0; kk < Cfg::P / 16; ++kk) {
+              const uint64_t bd = umma_desc_sw128(w1 + (kk >> 2) * (Cfg::HD * 128) + nh * (Cfg::HD / 2) * 128 + (kk & 3) * 32);
 #pragma unroll
-            for (int part = 0; part < Cfg::ZPARTS; ++part)
-              umma_bf16_ts(tmem + Cfg::ACC_COL, zcol + part * (Cfg::HD / 2) + kk * 8, bd, id2,
-                           (kk | part) != 0);
+              for (int part = 0; part < Cfg::ZPARTS; ++part)
+                umma_bf16_ts(tmem + Cfg::ACC_COL + nh * (Cfg::HD / 2), zcol + part * (Cfg::P / 2) + kk * 8, bd,
+                             id1, (kk | part) != 0);
+            }
+            if (Cfg::H_IN_ACC) umma_commit(&bars[nh == 0 ? BAR_ACC_FULL : BAR_ACC_FULL_B]);
           }
+          if (Cfg::H_IN_ACC) {
+            umma_commit(&bars[BAR_Z_EMPTY + slot]);
+          } else {
+            umma_commit(&bars[BAR_ACC_FULL]);
+            umma_commit(&bars[BAR_ACC_FULL_B]);
+          }
+          // GEMM2 in two K halves, each as soon as its half of h is in tensor memory.
+#pragma unroll 1
+          for (int kh = 0; kh < 2; ++kh) {
+            if (!mbar_wait(&bars[kh == 0 ? BAR_H_FULL : BAR_H_FULL_B], (uint32_t)it & 1, fs, W_MMA_HFULL)) { ok = false; break; }
+            tc_fence_after();
+#pragma unroll 1
+            for (int kk = kh * (Cfg::HD / 32); kk < (kh + 1) * (Cfg::HD / 32); ++kk) {
+              const uint64_t bd = umma_desc_sw128(w2 + (kk >> 2) * (Cfg::C * 128) + (kk & 3) * 32);
+              if constexpr (Cfg::H_IN_ACC) {
+                const uint32_t a = tmem + Cfg::ACC_COL + kh * (Cfg::HD / 2) + (kk - kh * (Cfg::HD / 32)) * 8;
+                umma_bf16_ts(tmem + Cfg::ACC2_COL, a, bd, id2, kk != 0);
+              } else {
+#pragma unroll
+                for (int part = 0; part < Cfg::ZPARTS; ++part)
+                  umma_bf16_ts(tmem + Cfg::ACC2_COL, zcol + part * (Cfg::HD / 2) + kk * 8, bd, id2,
+                               (kk | part) != 0);
+              }
+            }
+          }
+          if (!ok) break;
           umma_commit(&bars[BAR_ACC2_FULL]);
-          umma_commit(&bars[BAR_Z_EMPTY + slot]);
+          if (!Cfg::H_IN_ACC) umma_commit(&bars[BAR_Z_EMPTY + slot]);
         }
       }
       // Drain: every MMA issued above has completed once this commit arrives.
@@ -345,22 +372,44 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         const int stage = (int)(it % S);
         const uint32_t v = (uint32_t)(it / S);
         if (!warp_wait(&bars[BAR_WIN_EMPTY + stage], (v & 1) ^ 1, fs, W_LOAD_EMPTY)) { ok = false; break; }
-        const long long wb = t * kTileM - W - 1;
-        const uint32_t dst = smem_u32(smem + L.win + stage * WC * Cfg::ROWB);
-        for (int idx = lane; idx < WC * NCH; idx += 32) {
-          const int ch = idx / WC;
-          const int wc = idx - ch * WC;
-          const long long gs = wb + wc;
-          const bool in_range = gs >= 0 && gs < total;
-          const long long gcl = in_range ? gs : 0;
-          const uint8_t* p = src + ((((gcl >> 7) * NCH + ch) << 7) + (gcl & 127)) * 16;
-          cp_async_16(dst + wc * Cfg::ROWB + ((ch ^ win_swz<Cfg::NCH>(wc)) << 4), p,
-                      in_range ? 16u : 0u);
+        // the old fp32 state of tile t (read by the epilogue) into L2: one contiguous block
+        if (lane == 31) {
+          const float* blk = A.master[in] + t * (kTileM * Cfg::C);
+          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(blk), "r"((uint32_t)(kTileM * Cfg::C * 4))
+                       : "memory");
         }
-        cp_async_mbar_arrive_noinc(&bars[BAR_WIN_FULL + stage]);
+        const long long wb = t * kTileM - W - 1;
+        const long long lo = wb < 0 ? 0 : wb;
+        const long long hi = (wb + WC) < total ? (wb + WC) : total;
+        if (lane == 0) mbar_arrive_expect_tx(&bars[BAR_WIN_FULL + stage], (uint32_t)(NCH * (hi - lo) * 16));
+        __syncwarp();
+        const uint32_t dst = smem_u32(smem + L.win + stage * WC * Cfg::ROWB);
+        // one bulk copy per (chunk, tile overlapped by the window): at most 3 tiles
+        const long long t0 = lo >> 7;
+        for (int job = lane; job < NCH * 3; job += 32) {
+          const int ch = job / 3;
+          const long long T = t0 + job % 3;
+          const long long c_lo = (T << 7) > lo ? (T << 7) : lo;
+          const long long c_hi = ((T + 1) << 7) < hi ? ((T + 1) << 7) : hi;
+          if (c_hi > c_lo) {
+            const uint8_t* p = src + (((T * NCH + ch) << 7) + (c_lo & 127)) * 16;
+            bulk_g2s(dst + (uint32_t)((ch * WC + (c_lo - wb)) * 16), p, (uint32_t)((c_hi - c_lo) * 16),
+                     &bars[BAR_WIN_FULL + stage]);
+          }
+        }
       }
     }
-    cp_async_wait_all();
+    // Bulk copies still in flight (only after an abort) must land before the CTA exits.
+    if (lane == 0) {
+      for (int sg = 0; sg < S && sg < it; ++sg) {
+        const long long last = ((it - 1 - sg) / S) * S + sg;  // last tile index issued on stage sg
+        const uint32_t par = (uint32_t)(last / S) & 1;
+        const uint64_t t0 = global_timer_ns();
+        while (!mbar_try_wait(&bars[BAR_WIN_FULL + sg], par)) {
+          if (global_timer_ns() - t0 > fs.timeout_ns) { report_failure(fs, 4, W_DRAIN); break; }
+        }
+      }
+    }
     __syncwarp();
   } else if (!skip && warp >= kStencilWarp0 && warp < kEpiWarp0) {
     // ---------------------------------------------------------------- stencil
@@ -395,61 +444,86 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         const bool lf = valid && j > 0, rt = valid && j < W - 1;
         const int c0 = m + W + 1;  // window index of this cell
         const uint32_t zbase = tmem + lane_addr + slot * Cfg::SLOT_COLS;
+        // the 9 neighbours a b c / d e f / g h k: their cell offsets in the window stage
+        const uint32_t wbase = smem_u32(win);
+        uint32_t nb_row[9];
+        bool nb_ok[9];
+#pragma unroll
+        for (int n = 0; n < 9; ++n) {
+          const int dy = n / 3 - 1, dx = n % 3 - 1;
+          const int wc = c0 + dy * W + dx;
+          nb_ok[n] = (dy < 0 ? up : (dy > 0 ? dn : valid)) && (dx < 0 ? lf : (dx > 0 ? rt : true));
+          nb_row[n] = wbase + (uint32_t)(nb_ok[n] ? wc : 0) * 16u;
+        }
 #pragma unroll 1
         for (int q = 0; q < Cfg::NCH / 2; ++q) {
           const int ch = half * (Cfg::NCH / 2) + q;
-          auto ld = [&](bool ok_, int wc) -> uint4 {
-            uint4 r = make_uint4(0u, 0u, 0u, 0u);
-            if (ok_) r = *reinterpret_cast<const uint4*>(win + wc * Cfg::ROWB + ((ch ^ win_swz<Cfg::NCH>(wc)) << 4));
-            return r;
-          };
-          const uint4 va = ld(up && lf, c0 - W - 1), vb = ld(up, c0 - W), vc = ld(up && rt, c0 - W + 1);
-          const uint4 vd = ld(lf, c0 - 1), ve = ld(valid, c0), vf = ld(rt, c0 + 1);
-          const uint4 vg = ld(dn && lf, c0 + W - 1), vh = ld(dn, c0 + W), vk = ld(dn && rt, c0 + W + 1);
+          const uint32_t choff = (uint32_t)(ch * WC) * 16u;
+          uint4 v[9];
+#pragma unroll
+          for (int n = 0; n < 9; ++n) {
+            v[n] = make_uint4(0u, 0u, 0u, 0u);
+            if (nb_ok[n]) {
+              asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                           : "=r"(v[n].x), "=r"(v[n].y), "=r"(v[n].z), "=r"(v[n].w)
+                           : "r"(nb_row[n] + choff));
+            }
+          }
           if constexpr (Cfg::SRC_BF16) {
-            // 8 channels: ch*8 .. ch*8+7
-            const uint32_t* A_ = &va.x; const uint32_t* B_ = &vb.x; const uint32_t* C_ = &vc.x;
-            const uint32_t* D_ = &vd.x; const uint32_t* E_ = &ve.x; const uint32_t* F_ = &vf.x;
-            const uint32_t* G_ = &vg.x; const uint32_t* H_ = &vh.x; const uint32_t* K_ = &vk.x;
+            // 8 channels ch*8 .. ch*8+7 as 4 bf16 pairs; identity, Sobel-x, Sobel-y, Laplacian
             uint32_t zi[4], zx[4], zy[4], zl[4];
+            if (A.fixed_taps) {
+              const float2 two = f2(2.f, 2.f), mone = f2(-1.f, -1.f), m16 = f2(-16.f, -16.f);
+              const float2 k8 = f2(0.125f, 0.125f), k16 = f2(0.0625f, 0.0625f);
 #pragma unroll
-            for (int w = 0; w < 4; ++w) {
-              float o[2][3];
+              for (int w = 0; w < 4; ++w) {
+                const uint32_t* vw = &v[0].x;
+                const float2 a = unpack_bf16x2((&v[0].x)[w]), b = unpack_bf16x2((&v[1].x)[w]);
+                const float2 c = unpack_bf16x2((&v[2].x)[w]), d = unpack_bf16x2((&v[3].x)[w]);
+                const float2 e = unpack_bf16x2((&v[4].x)[w]), f = unpack_bf16x2((&v[5].x)[w]);
+                const float2 g = unpack_bf16x2((&v[6].x)[w]), h = unpack_bf16x2((&v[7].x)[w]);
+                const float2 k = unpack_bf16x2((&v[8].x)[w]);
+                (void)vw;
+                // column sums S = top + 2 mid + bottom, column differences D = bottom - top
+                const float2 sl = __fadd2_rn(__ffma2_rn(two, d, a), g);
+                const float2 sm = __fadd2_rn(__ffma2_rn(two, e, b), h);
+                const float2 sr = __fadd2_rn(__ffma2_rn(two, f, c), k);
+                const float2 dl = __ffma2_rn(mone, a, g);
+                const float2 dm = __ffma2_rn(mone, b, h);
+                const float2 dr = __ffma2_rn(mone, c, k);
+                const float2 sx = __fmul2_rn(__ffma2_rn(mone, sl, sr), k8);
+                const float2 sy = __fmul2_rn(__fadd2_rn(__ffma2_rn(two, dm, dl), dr), k8);
+                const float2 lp = __fmul2_rn(__ffma2_rn(m16, e, __fadd2_rn(__ffma2_rn(two, sm, sl), sr)), k16);
+                zi[w] = (&v[4].x)[w];  // identity head of a bf16 source is the value itself
+                zx[w] = pack_bf16(sx.x, sx.y);
+                zy[w] = pack_bf16(sy.x, sy.y);
+                zl[w] = pack_bf16(lp.x, lp.y);
+              }
+            } else {
 #pragma unroll
-              for (int e = 0; e < 2; ++e) {
-                auto cv = [&](uint32_t x) { return e == 0 ? bf16lo_to_f32(x) : bf16hi_to_f32(x); };
-                if (A.fixed_taps) {
-                  fixed_taps4(cv(A_[w]), cv(B_[w]), cv(C_[w]), cv(D_[w]), cv(E_[w]), cv(F_[w]),
-                              cv(G_[w]), cv(H_[w]), cv(K_[w]), o[e][0], o[e][1], o[e][2]);
-                } else {
-                  const float nb[9] = {cv(A_[w]), cv(B_[w]), cv(C_[w]), cv(D_[w]), cv(E_[w]),
-                                       cv(F_[w]), cv(G_[w]), cv(H_[w]), cv(K_[w])};
+              for (int w = 0; w < 4; ++w) {
+                float o[4][2];
 #pragma unroll
-                  for (int kh = 1; kh < 4; ++kh) {
+                for (int e = 0; e < 2; ++e) {
+                  float nb[9];
+#pragma unroll
+                  for (int n = 0; n < 9; ++n) {
+                    const uint32_t x = (&v[n].x)[w];
+                    nb[n] = e == 0 ? bf16lo_to_f32(x) : bf16hi_to_f32(x);
+                  }
+#pragma unroll
+                  for (int kh = 0; kh < 4; ++kh) {
                     float acc = 0.f;
 #pragma unroll
                     for (int n = 0; n < 9; ++n) acc = fmaf(A.taps[kh][n], nb[n], acc);
-                    o[e][kh - 1] = acc;
+                    o[kh][e] = acc;
                   }
                 }
+                zi[w] = pack_bf16(o[0][0], o[0][1]);
+                zx[w] = pack_bf16(o[1][0], o[1][1]);
+                zy[w] = pack_bf16(o[2][0], o[2][1]);
+                zl[w] = pack_bf16(o[3][0], o[3][1]);
               }
-              if (A.fixed_taps) {
-                zi[w] = E_[w];  // identity head of a bf16 source is the value itself
-              } else {
-                const float nb0[9] = {bf16lo_to_f32(A_[w]), bf16lo_to_f32(B_[w]), bf16lo_to_f32(C_[w]),
-                                      bf16lo_to_f32(D_[w]), bf16lo_to_f32(E_[w]), bf16lo_to_f32(F_[w]),
-                                      bf16lo_to_f32(G_[w]), bf16lo_to_f32(H_[w]), bf16lo_to_f32(K_[w])};
-                const float nb1[9] = {bf16hi_to_f32(A_[w]), bf16hi_to_f32(B_[w]), bf16hi_to_f32(C_[w]),
-                                      bf16hi_to_f32(D_[w]), bf16hi_to_f32(E_[w]), bf16hi_to_f32(F_[w]),
-                                      bf16hi_to_f32(G_[w]), bf16hi_to_f32(H_[w]), bf16hi_to_f32(K_[w])};
-                float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-                for (int n = 0; n < 9; ++n) { a0 = fmaf(A.taps[0][n], nb0[n], a0); a1 = fmaf(A.taps[0][n], nb1[n], a1); }
-                zi[w] = pack_bf16(a0, a1);
-              }
-              zx[w] = pack_bf16(o[0][0], o[1][0]);
-              zy[w] = pack_bf16(o[0][1], o[1][1]);
-              zl[w] = pack_bf16(o[0][2], o[1][2]);
             }
             const int cb = ch * 8;  // first channel of the chunk
             tmem_st4(zbase + (0 * Cfg::C + cb) / 2, zi);
@@ -458,20 +532,17 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
             tmem_st4(zbase + (3 * Cfg::C + cb) / 2, zl);
           } else {
             // fp32 source, 4 channels: ch*4 .. ch*4+3; z split into bf16 hi + lo parts
-            const float* A_ = reinterpret_cast<const float*>(&va); const float* B_ = reinterpret_cast<const float*>(&vb);
-            const float* C_ = reinterpret_cast<const float*>(&vc); const float* D_ = reinterpret_cast<const float*>(&vd);
-            const float* E_ = reinterpret_cast<const float*>(&ve); const float* F_ = reinterpret_cast<const float*>(&vf);
-            const float* G_ = reinterpret_cast<const float*>(&vg); const float* H_ = reinterpret_cast<const float*>(&vh);
-            const float* K_ = reinterpret_cast<const float*>(&vk);
             float z[4][4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
+              float nb[9];
+#pragma unroll
+              for (int n = 0; n < 9; ++n) nb[n] = __uint_as_float((&v[n].x)[e]);
               if (A.fixed_taps) {
-                z[0][e] = E_[e];
-                fixed_taps4(A_[e], B_[e], C_[e], D_[e], E_[e], F_[e], G_[e], H_[e], K_[e], z[1][e],
+                z[0][e] = nb[4];
+                fixed_taps4(nb[0], nb[1], nb[2], nb[3], nb[4], nb[5], nb[6], nb[7], nb[8], z[1][e],
                             z[2][e], z[3][e]);
               } else {
-                const float nb[9] = {A_[e], B_[e], C_[e], D_[e], E_[e], F_[e], G_[e], H_[e], K_[e]};
 #pragma unroll
                 for (int kh = 0; kh < 4; ++kh) {
                   float acc = 0.f;
@@ -524,8 +595,50 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         const int slot = (int)(it % Cfg::NZ);
         const uint32_t zbase = tmem + lane_addr + slot * Cfg::SLOT_COLS;
         const uint32_t abase = tmem + lane_addr + Cfg::ACC_COL;
+        // ---- before E1: the given flag and the fire decision, computed while GEMM1 runs.
+        const long long g = t * kTileM + m;
+        const bool valid = g < total;
+        int inst = 0, p = 0, row = 0;
+        if (valid) {
+          inst = (int)(g / A.HW);
+          p = (int)(g - (long long)inst * A.HW);
+          row = A.inst_row ? A.inst_row[inst] : inst / A.K;
+        }
+        const bool gv = valid && A.given[(long long)row * A.HW + p] != 0;
+        // fire decision (needs the old state for the adaptive rule)
+        float f = 0.f;
+        if (valid) {
+          if (A.fire_mode == 0) {
+            f = A.masks[((long long)s * A.n_inst + inst) * A.HW + p] ? 1.f : 0.f;
+          } else {
+            float prob = A.p_fire;
+            if (A.fire_mode >= 2) {
+              float xo_[16];
+              for (int c = 0; c < A.c_out; ++c) {
+                const int cc = A.out_off + c;
+                xo_[c] = xin[(((t * (Cfg::C / 4) + (cc >> 2)) << 7) + m) * 4 + (cc & 3)];
+              }
+              float sc[16];
+              float mx = -3.402823466e38f;
+              for (int o = 0; o < A.n_out; ++o) {
+                float a = A.head_b[o];
+                for (int c = 0; c < A.c_out; ++c) a = fmaf(A.head_w[o][c], xo_[c], a);
+                sc[o] = a;
+                mx = fmaxf(mx, a);
+              }
+              float den = 0.f;
+              for (int o = 0; o < A.n_out; ++o) den += expf(sc[o] - mx);
+              float conf = fminf(fmaxf(1.f / den, 0.f), 1.f);
+              prob = A.ad_scale * (1.f - conf) + A.ad_bias;
+            }
+            float uu;
+            if (A.fire_mode == 3) uu = A.uniforms[((long long)s * A.n_inst + inst) * A.HW + p];
+            else uu = philox_uniform(A.seed, A.inst_offset + inst, p, step);
+            f = (uu < prob) ? 1.f : 0.f;
+          }
+        }
         // ---- E1: hidden = relu(acc1 + b1) -> bf16 into the z slot
-        if (!warp_wait(&bars[BAR_ACC_FULL], (uint32_t)it & 1, fs, W_E1_ACC)) { ok = false; break; }
+        if (!warp_wait(&bars[half == 0 ? BAR_ACC_FULL : BAR_ACC_FULL_B], (uint32_t)it & 1, fs, W_E1_ACC)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll 1
         for (int cbk = 0; cbk < Cfg::HD / 2; cbk += 32) {
@@ -533,13 +646,18 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           uint32_t r[32];
           tmem_ld32(abase + col, r);
           tc_wait_ld();
+          const float4* bb = reinterpret_cast<const float4*>(s_b1 + col);
           uint32_t hi[16];
           if constexpr (!Cfg::SPLIT) {
 #pragma unroll
-            for (int q = 0; q < 16; ++q)
-              hi[q] = pack_bf16_relu(__uint_as_float(r[2 * q]) + s_b1[col + 2 * q],
-                                     __uint_as_float(r[2 * q + 1]) + s_b1[col + 2 * q + 1]);
-            tmem_st16(zbase + col / 2, hi);
+            for (int q = 0; q < 8; ++q) {
+              const float4 b = bb[q];
+              const float2 h0 = __fadd2_rn(f2(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1])), f2(b.x, b.y));
+              const float2 h1 = __fadd2_rn(f2(__uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])), f2(b.z, b.w));
+              hi[2 * q] = pack_bf16_relu(h0.x, h0.y);
+              hi[2 * q + 1] = pack_bf16_relu(h1.x, h1.y);
+            }
+            tmem_st16(abase + half * (Cfg::HD / 2) + cbk / 2, hi);  // over the columns already read
           } else {
             uint32_t lo[16];
 #pragma unroll
@@ -556,93 +674,60 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[BAR_H_FULL]);
+        if (lane == 0) mbar_arrive(&bars[half == 0 ? BAR_H_FULL : BAR_H_FULL_B]);
 
-        // ---- E2: dx = acc2 + b2; x' = x + f * dx; clamp; store
-        const long long g = t * kTileM + m;
-        const bool valid = g < total;
-        int inst = 0, p = 0, row = 0;
-        if (valid) {
-          inst = (int)(g / A.HW);
-          p = (int)(g - (long long)inst * A.HW);
-          row = A.inst_row ? A.inst_row[inst] : inst / A.K;
-        }
-        // fire decision (needs the old state for the adaptive rule)
-        float f = 0.f;
-        if (valid) {
-          if (A.fire_mode == 0) {
-            f = A.masks[((long long)s * A.n_inst + inst) * A.HW + p] ? 1.f : 0.f;
-          } else {
-            float prob = A.p_fire;
-            if (A.fire_mode >= 2) {
-              float xo[16];
-              for (int c = 0; c < A.c_out; ++c) {
-                const int cc = A.out_off + c;
-                xo[c] = xin[(((t * (Cfg::C / 4) + (cc >> 2)) << 7) + m) * 4 + (cc & 3)];
-              }
-              float sc[16];
-              float mx = -3.402823466e38f;
-              for (int o = 0; o < A.n_out; ++o) {
-                float a = A.head_b[o];
-                for (int c = 0; c < A.c_out; ++c) a = fmaf(A.head_w[o][c], xo[c], a);
-                sc[o] = a;
-                mx = fmaxf(mx, a);
-              }
-              float den = 0.f;
-              for (int o = 0; o < A.n_out; ++o) den += expf(sc[o] - mx);
-              float conf = fminf(fmaxf(1.f / den, 0.f), 1.f);
-              prob = A.ad_scale * (1.f - conf) + A.ad_bias;
-            }
-            float uu;
-            if (A.fire_mode == 3) uu = A.uniforms[((long long)s * A.n_inst + inst) * A.HW + p];
-            else uu = philox_uniform(A.seed, A.inst_offset + inst, p, step);
-            f = (uu < prob) ? 1.f : 0.f;
-          }
-        }
+        // ---- E2: dx = acc2 + b2; x' = x + f * dx; clamp; store.  The old state of this thread's
+        // channels is loaded while GEMM2 runs (the loader prefetched the tile into L2).
+        constexpr int NQ = CH / 4;  // float4 chunks of this thread
+        float4 xo[NQ];
+        const float4* xin4 = reinterpret_cast<const float4*>(xin) + ((t * (Cfg::C / 4) + half * NQ) << 7) + m;
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) xo[q] = valid ? __ldg(xin4 + (q << 7)) : make_float4(0.f, 0.f, 0.f, 0.f);
         if (!warp_wait(&bars[BAR_ACC2_FULL], (uint32_t)it & 1, fs, W_E2_ACC2)) { ok = false; break; }
         tc_fence_after();
         uint32_t r[CH];
         if constexpr (CH == 32) {
-          tmem_ld32(abase + half * CH, r);
+          tmem_ld32(abase + (Cfg::ACC2_COL - Cfg::ACC_COL) + half * CH, r);
         } else {
-          tmem_ld16(abase + half * CH, *reinterpret_cast<uint32_t(*)[16]>(r));
+          tmem_ld16(abase + (Cfg::ACC2_COL - Cfg::ACC_COL) + half * CH, *reinterpret_cast<uint32_t(*)[16]>(r));
         }
         tc_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[BAR_ACC_EMPTY]);
         if (valid) {
-          const bool gv = A.given[(long long)row * A.HW + p] != 0;
           const float* clamp_row = A.clamp + ((long long)row * A.HW + p) * A.c_in;
+          const float4* bb = reinterpret_cast<const float4*>(s_b2 + half * CH);
+          const float2 ff = f2(f, f);
+          float4* xout4 = reinterpret_cast<float4*>(xout) + ((t * (Cfg::C / 4) + half * NQ) << 7) + m;
+          uint32_t pk[CH / 2];
 #pragma unroll
-          for (int q = 0; q < CH / 8; ++q) {
-            float xn[8];
-#pragma unroll
-            for (int hq = 0; hq < 2; ++hq) {
-              const int c4 = (half * CH) / 4 + q * 2 + hq;   // float4 chunk index
-              const float4 xo = *reinterpret_cast<const float4*>(xin + (((t * (Cfg::C / 4) + c4) << 7) + m) * 4);
-              const float xv[4] = {xo.x, xo.y, xo.z, xo.w};
+          for (int q = 0; q < NQ; ++q) {
+            const float4 b = bb[q];
+            const float2 d0 = __fadd2_rn(f2(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1])), f2(b.x, b.y));
+            const float2 d1 = __fadd2_rn(f2(__uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])), f2(b.z, b.w));
+            float2 y0 = __ffma2_rn(ff, d0, f2(xo[q].x, xo[q].y));
+            float2 y1 = __ffma2_rn(ff, d1, f2(xo[q].z, xo[q].w));
+            const int c0_ = half * CH + 4 * q;  // first channel of this chunk
+            if (gv && c0_ + 4 > A.in_off && c0_ < A.in_off + A.c_in) {
+              float y[4] = {y0.x, y0.y, y1.x, y1.y};
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                const int c = c4 * 4 + e;
-                const float dx = __uint_as_float(r[q * 8 + hq * 4 + e]) + s_b2[c];
-                float y = fmaf(f, dx, xv[e]);
-                const int ci = c - A.in_off;
-                if (gv && ci >= 0 && ci < A.c_in) y = clamp_row[ci];
-                xn[hq * 4 + e] = y;
+                const int ci = c0_ + e - A.in_off;
+                if (ci >= 0 && ci < A.c_in) y[e] = clamp_row[ci];
               }
-              *reinterpret_cast<float4*>(xout + (((t * (Cfg::C / 4) + c4) << 7) + m) * 4) =
-                  make_float4(xn[hq * 4 + 0], xn[hq * 4 + 1], xn[hq * 4 + 2], xn[hq * 4 + 3]);
+              y0 = f2(y[0], y[1]);
+              y1 = f2(y[2], y[3]);
             }
-            if constexpr (Cfg::SRC_BF16) {
-              const int c8 = (half * CH) / 8 + q;
-              uint4 pk;
-              pk.x = pack_bf16(xn[0], xn[1]);
-              pk.y = pack_bf16(xn[2], xn[3]);
-              pk.z = pack_bf16(xn[4], xn[5]);
-              pk.w = pack_bf16(xn[6], xn[7]);
-              *reinterpret_cast<uint4*>(mout + (((t * (Cfg::C / 8) + c8) << 7) + m) * 8) = pk;
-            }
+            xout4[q << 7] = make_float4(y0.x, y0.y, y1.x, y1.y);
+            pk[2 * q] = pack_bf16(y0.x, y0.y);
+            pk[2 * q + 1] = pack_bf16(y1.x, y1.y);
+          }
+          if constexpr (Cfg::SRC_BF16) {
+            uint4* mout4 = reinterpret_cast<uint4*>(mout) + ((t * (Cfg::C / 8) + half * (CH / 8)) << 7) + m;
+#pragma unroll
+            for (int q = 0; q < CH / 8; ++q)
+              mout4[q << 7] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
           }
         }
         if (half == 0 && A.updates != nullptr) {

@@ -332,7 +332,11 @@ int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaState* st,
   A.W = b->width;
   A.HW = b->height * b->width;
   A.K = b->trials;
+  A.div_hw = make_fastdiv((unsigned)A.HW);
+  A.div_w = make_fastdiv((unsigned)A.W);
+  A.div_k = make_fastdiv((unsigned)A.K);
   A.total = (long long)b->n_inst * A.HW;
+  if (A.total + 2 * kTileM + 2LL * A.W >= (1LL << 31)) return NCA_ERR_UNSUPPORTED;  // 32-bit cell ids
   A.n_tiles = st->n_tiles;
   A.inst_offset = b->inst_offset;
   A.n_steps = n_steps;

@@ -18,6 +18,8 @@
 // region holding acc1 (then acc2 in its first C columns).  Every wait is bounded; a wait that
 // runs out records NCA_ERR_TIMEOUT in the control words and the CTA drains and exits.
 #pragma once
+#include <cuda_bf16.h>
+
 #include "ptx.cuh"
 
 namespace nca {
@@ -65,8 +67,26 @@ struct StepCfg {
   static_assert(!H_IN_ACC || C <= HD / 4, "acc2 must fit next to h in the accumulator region");
 };
 
+// n / d for 0 <= n < 2^31 with a multiply-high and a shift (Granlund & Montgomery, "Division by
+// invariant integers using multiplication", PLDI'94): q = (umulhi(n, m) + n) >> l with
+// l = ceil(log2 d) and m = floor(2^32 (2^l - d) / d) + 1.
+struct FastDiv {
+  unsigned m;
+  int l;
+};
+__host__ __device__ __forceinline__ FastDiv make_fastdiv(unsigned d) {
+  int l = 0;
+  while ((1ull << l) < d) ++l;
+  FastDiv f;
+  f.m = (unsigned)((((1ull << 32) * ((1ull << l) - d)) / d) + 1);
+  f.l = l;
+  return f;
+}
+__device__ __forceinline__ unsigned fdiv(unsigned n, FastDiv f) { return (__umulhi(n, f.m) + n) >> f.l; }
+
 struct StepArgs {
   int n_inst, H, W, HW, K;
+  FastDiv div_hw, div_w, div_k;
   long long total, n_tiles, inst_offset;
   int n_steps;
   long long step0;
@@ -97,15 +117,16 @@ struct StepArgs {
 // Shared-memory layout (offsets from a 1024-byte aligned base).
 template <class Cfg>
 struct SmemLayout {
-  int w1, w2, win, b1, b2, bars, misc, total;
+  int w1, w2, win, b1, b2, flags, bars, misc, total;
   __host__ __device__ SmemLayout(int stages, int win_cells) {
     w1 = 0;
     w2 = w1 + Cfg::W1_BYTES;
     win = (w2 + Cfg::W2_BYTES + 1023) & ~1023;
     b1 = (win + stages * win_cells * Cfg::ROWB + 15) & ~15;
     b2 = b1 + Cfg::HD * 4;
-    bars = (b2 + Cfg::C * 4 + 7) & ~7;
-    misc = bars + 16 * 8;
+    flags = b2 + Cfg::C * 4;
+    bars = (flags + 4 * kTileM + 7) & ~7;
+    misc = bars + 24 * 8;
     total = misc + 64;
   }
 };
@@ -123,12 +144,13 @@ enum BarId {
   BAR_DRAIN = 13,
   BAR_ACC_FULL_B = 14,  // second half of GEMM1 (hidden units HD/2 .. HD)
   BAR_H_FULL_B = 15,    // second half of the hidden epilogue
+  BAR_FLAGS = 16,       // +ring index (4): per-row fire/given flags of a tile are written
 };
 
 // Failure sites reported in ctrl[1].
 enum Where {
   W_MMA_ZFULL = 1, W_MMA_ACCEMPTY, W_MMA_HFULL, W_MMA_WEIGHTS, W_LOAD_EMPTY, W_LOAD_GRID,
-  W_ST_WINFULL, W_ST_ZEMPTY, W_E1_ACC, W_E2_ACC2, W_DRAIN
+  W_ST_WINFULL, W_ST_ZEMPTY, W_E1_ACC, W_E2_ACC2, W_DRAIN, W_E2_FLAGS
 };
 
 // A window stage is laid out [chunk][window cell][16 B]: lanes that read the same chunk of
@@ -162,6 +184,12 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
          ((uint64_t)(1024 >> 4) << 32) |                              // SBO = 1024 B
          ((uint64_t)1 << 46) |                                        // descriptor version
          ((uint64_t)2 << 61);                                         // SWIZZLE_128B
+}
+
+// The start-address field holds address >> 4 in the low 14 bits; shared memory is < 256 KB,
+// so adding (bytes >> 4) moves the start address without touching the other fields.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t bytes) {
+  return d + (uint64_t)(bytes >> 4);
 }
 
 __device__ __forceinline__ uint32_t idesc_bf16_f32(int M, int N) {
@@ -201,6 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
   int* abort_flag = reinterpret_cast<int*>(smem + L.misc + 8);
   float* s_b1 = reinterpret_cast<float*>(smem + L.b1);
   float* s_b2 = reinterpret_cast<float*>(smem + L.b2);
+  uint8_t* s_flags = smem + L.flags;  // [4][128]: bit0 fire, bit1 given, bit2 valid
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -227,6 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
     mbar_init(&bars[BAR_ACC_EMPTY], 8);
     mbar_init(&bars[BAR_WEIGHTS], 1);
     mbar_init(&bars[BAR_DRAIN], 1);
+    for (int r = 0; r < 4; ++r) mbar_init(&bars[BAR_FLAGS + r], 4);
     fence_mbar_init();
   }
   for (int i = threadIdx.x; i < Cfg::HD; i += kThreads) s_b1[i] = A.b1[i];
@@ -262,6 +292,8 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
       const uint32_t w1 = smem_u32(smem + L.w1);
       const uint32_t w2 = smem_u32(smem + L.w2);
       const uint32_t id1 = idesc_bf16_f32(kTileM, Cfg::HD / 2);
+      const uint64_t d1 = umma_desc_sw128(w1);
+      const uint64_t d2 = umma_desc_sw128(w2);
       const uint32_t id2 = idesc_bf16_f32(kTileM, Cfg::C);
       long long it = 0;
       for (int s = 0; ok && s < A.n_steps; ++s) {
@@ -274,16 +306,18 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           tc_fence_after();
           // GEMM1 in two N halves (hidden units [0, HD/2) then [HD/2, HD)).  In bf16 mode each half
           // is committed on its own, so that the hidden epilogue of the first half overlaps the
-          // second half, and the z slot is released right after GEMM1.
-#pragma unroll 1
+          // second half, and the z slot is released right after GEMM1.  The loops are unrolled
+          // and every descriptor is a constant offset of d1/d2, so one thread issues the MMAs
+          // faster than the tensor core retires them.
+#pragma unroll
           for (int nh = 0; nh < 2; ++nh) {
-#pragma unroll 1
+#pragma unroll
             for (int kk = 0; kk < Cfg::P / 16; ++kk) {
-              const uint64_t bd = umma_desc_sw128(w1 + (kk >> 2) * (Cfg::HD * 128) + nh * (Cfg::HD / 2) * 128 + (kk & 3) * 32);
+              const uint32_t boff = (kk >> 2) * (Cfg::HD * 128) + nh * (Cfg::HD / 2) * 128 + (kk & 3) * 32;
 #pragma unroll
               for (int part = 0; part < Cfg::ZPARTS; ++part)
-                umma_bf16_ts(tmem + Cfg::ACC_COL + nh * (Cfg::HD / 2), zcol + part * (Cfg::P / 2) + kk * 8, bd,
-                             id1, (kk | part) != 0);
+                umma_bf16_ts(tmem + Cfg::ACC_COL + nh * (Cfg::HD / 2), zcol + part * (Cfg::P / 2) + kk * 8,
+                             desc_add(d1, boff), id1, (kk | part) != 0);
             }
             if (Cfg::H_IN_ACC) umma_commit(&bars[nh == 0 ? BAR_ACC_FULL : BAR_ACC_FULL_B]);
           }
@@ -294,21 +328,22 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
             umma_commit(&bars[BAR_ACC_FULL_B]);
           }
           // GEMM2 in two K halves, each as soon as its half of h is in tensor memory.
-#pragma unroll 1
+#pragma unroll
           for (int kh = 0; kh < 2; ++kh) {
             if (!mbar_wait(&bars[kh == 0 ? BAR_H_FULL : BAR_H_FULL_B], (uint32_t)it & 1, fs, W_MMA_HFULL)) { ok = false; break; }
             tc_fence_after();
-#pragma unroll 1
-            for (int kk = kh * (Cfg::HD / 32); kk < (kh + 1) * (Cfg::HD / 32); ++kk) {
-              const uint64_t bd = umma_desc_sw128(w2 + (kk >> 2) * (Cfg::C * 128) + (kk & 3) * 32);
+#pragma unroll
+            for (int kq = 0; kq < Cfg::HD / 32; ++kq) {
+              const int kk = kh * (Cfg::HD / 32) + kq;
+              const uint32_t boff = (kk >> 2) * (Cfg::C * 128) + (kk & 3) * 32;
               if constexpr (Cfg::H_IN_ACC) {
-                const uint32_t a = tmem + Cfg::ACC_COL + kh * (Cfg::HD / 2) + (kk - kh * (Cfg::HD / 32)) * 8;
-                umma_bf16_ts(tmem + Cfg::ACC2_COL, a, bd, id2, kk != 0);
+                umma_bf16_ts(tmem + Cfg::ACC2_COL, tmem + Cfg::ACC_COL + kh * (Cfg::HD / 2) + kq * 8,
+                             desc_add(d2, boff), id2, kk != 0);
               } else {
 #pragma unroll
                 for (int part = 0; part < Cfg::ZPARTS; ++part)
-                  umma_bf16_ts(tmem + Cfg::ACC2_COL, zcol + part * (Cfg::HD / 2) + kk * 8, bd, id2,
-                               (kk | part) != 0);
+                  umma_bf16_ts(tmem + Cfg::ACC2_COL, zcol + part * (Cfg::HD / 2) + kk * 8, desc_add(d2, boff),
+                               id2, (kk | part) != 0);
               }
             }
           }
@@ -372,12 +407,6 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         const int stage = (int)(it % S);
         const uint32_t v = (uint32_t)(it / S);
         if (!warp_wait(&bars[BAR_WIN_EMPTY + stage], (v & 1) ^ 1, fs, W_LOAD_EMPTY)) { ok = false; break; }
-        // the old fp32 state of tile t (read by the epilogue) into L2: one contiguous block
-        if (lane == 31) {
-          const float* blk = A.master[in] + t * (kTileM * Cfg::C);
-          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(blk), "r"((uint32_t)(kTileM * Cfg::C * 4))
-                       : "memory");
-        }
         const long long wb = t * kTileM - W - 1;
         const long long lo = wb < 0 ? 0 : wb;
         const long long hi = (wb + WC) < total ? (wb + WC) : total;
@@ -432,13 +461,31 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         if (!warp_wait(&bars[BAR_Z_EMPTY + slot], (u & 1) ^ 1, fs, W_ST_ZEMPTY)) { ok = false; break; }
         tc_fence_after();
         const uint8_t* win = smem + L.win + stage * WC * Cfg::ROWB;
-        const long long g = t * kTileM + m;
-        const bool valid = g < total;
-        int i = 0, j = 0;
+        const unsigned g = (unsigned)t * kTileM + m;
+        const bool valid = (long long)g < total;
+        int i = 0, j = 0, inst = 0, p = 0;
         if (valid) {
-          const int p = (int)(g % A.HW);
-          i = p / W;
+          inst = (int)fdiv(g, A.div_hw);
+          p = (int)(g - (unsigned)inst * A.HW);
+          i = (int)fdiv((unsigned)p, A.div_w);
           j = p - i * W;
+        }
+        if (half == 0) {
+          // per-row side information for the epilogue: given flag and (except for the adaptive
+          // rules, which need the fp32 state) the fire decision of this step
+          uint32_t fl = 0;
+          if (valid) {
+            const int row = A.inst_row ? A.inst_row[inst] : (int)fdiv((unsigned)inst, A.div_k);
+            fl = 4u | (A.given[(long long)row * A.HW + p] ? 2u : 0u);
+            if (A.fire_mode == 0) {
+              fl |= A.masks[((long long)s * A.n_inst + inst) * A.HW + p] ? 1u : 0u;
+            } else if (A.fire_mode == 1) {
+              fl |= philox_uniform(A.seed, A.inst_offset + inst, p, A.step0 + s) < A.p_fire ? 1u : 0u;
+            }
+          }
+          s_flags[(it & 3) * kTileM + m] = (uint8_t)fl;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars[BAR_FLAGS + (it & 3)]);
         }
         const bool up = valid && i > 0, dn = valid && i < A.H - 1;
         const bool lf = valid && j > 0, rt = valid && j < W - 1;
@@ -473,31 +520,27 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
             // 8 channels ch*8 .. ch*8+7 as 4 bf16 pairs; identity, Sobel-x, Sobel-y, Laplacian
             uint32_t zi[4], zx[4], zy[4], zl[4];
             if (A.fixed_taps) {
-              const float2 two = f2(2.f, 2.f), mone = f2(-1.f, -1.f), m16 = f2(-16.f, -16.f);
-              const float2 k8 = f2(0.125f, 0.125f), k16 = f2(0.0625f, 0.0625f);
+              // packed bf16x2 arithmetic (two channels per instruction, each operation rounded to
+              // bf16): column sums S = top + 2 mid + bottom and differences D = bottom - top of the
+              // left, middle and right columns give the three heads.
+              const __nv_bfloat162 two = __float2bfloat162_rn(2.f), k8 = __float2bfloat162_rn(0.125f);
+              const __nv_bfloat162 k16 = __float2bfloat162_rn(0.0625f), m16 = __float2bfloat162_rn(-16.f);
 #pragma unroll
               for (int w = 0; w < 4; ++w) {
-                const uint32_t* vw = &v[0].x;
-                const float2 a = unpack_bf16x2((&v[0].x)[w]), b = unpack_bf16x2((&v[1].x)[w]);
-                const float2 c = unpack_bf16x2((&v[2].x)[w]), d = unpack_bf16x2((&v[3].x)[w]);
-                const float2 e = unpack_bf16x2((&v[4].x)[w]), f = unpack_bf16x2((&v[5].x)[w]);
-                const float2 g = unpack_bf16x2((&v[6].x)[w]), h = unpack_bf16x2((&v[7].x)[w]);
-                const float2 k = unpack_bf16x2((&v[8].x)[w]);
-                (void)vw;
-                // column sums S = top + 2 mid + bottom, column differences D = bottom - top
-                const float2 sl = __fadd2_rn(__ffma2_rn(two, d, a), g);
-                const float2 sm = __fadd2_rn(__ffma2_rn(two, e, b), h);
-                const float2 sr = __fadd2_rn(__ffma2_rn(two, f, c), k);
-                const float2 dl = __ffma2_rn(mone, a, g);
-                const float2 dm = __ffma2_rn(mone, b, h);
-                const float2 dr = __ffma2_rn(mone, c, k);
-                const float2 sx = __fmul2_rn(__ffma2_rn(mone, sl, sr), k8);
-                const float2 sy = __fmul2_rn(__fadd2_rn(__ffma2_rn(two, dm, dl), dr), k8);
-                const float2 lp = __fmul2_rn(__ffma2_rn(m16, e, __fadd2_rn(__ffma2_rn(two, sm, sl), sr)), k16);
+                auto B2 = [&](int n) { return *reinterpret_cast<const __nv_bfloat162*>(&v[n].x + w); };
+                const __nv_bfloat162 a = B2(0), b = B2(1), c = B2(2), d = B2(3), e = B2(4);
+                const __nv_bfloat162 f = B2(5), g = B2(6), h = B2(7), k = B2(8);
+                const __nv_bfloat162 sl = __hadd2(__hfma2(two, d, a), g);
+                const __nv_bfloat162 sm = __hadd2(__hfma2(two, e, b), h);
+                const __nv_bfloat162 sr = __hadd2(__hfma2(two, f, c), k);
+                const __nv_bfloat162 dl = __hsub2(g, a), dm = __hsub2(h, b), dr = __hsub2(k, c);
+                const __nv_bfloat162 sx = __hmul2(__hsub2(sr, sl), k8);
+                const __nv_bfloat162 sy = __hmul2(__hadd2(__hfma2(two, dm, dl), dr), k8);
+                const __nv_bfloat162 lp = __hmul2(__hfma2(m16, e, __hadd2(__hfma2(two, sm, sl), sr)), k16);
                 zi[w] = (&v[4].x)[w];  // identity head of a bf16 source is the value itself
-                zx[w] = pack_bf16(sx.x, sx.y);
-                zy[w] = pack_bf16(sy.x, sy.y);
-                zl[w] = pack_bf16(lp.x, lp.y);
+                zx[w] = *reinterpret_cast<const uint32_t*>(&sx);
+                zy[w] = *reinterpret_cast<const uint32_t*>(&sy);
+                zl[w] = *reinterpret_cast<const uint32_t*>(&lp);
               }
             } else {
 #pragma unroll
@@ -569,8 +612,8 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&bars[BAR_Z_FULL + slot]);
-          mbar_arrive(&bars[BAR_WIN_EMPTY + stage]);
+          mbar_arrive_relaxed(&bars[BAR_Z_FULL + slot]);
+          mbar_arrive_relaxed(&bars[BAR_WIN_EMPTY + stage]);
         }
       }
     }
@@ -595,47 +638,40 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         const int slot = (int)(it % Cfg::NZ);
         const uint32_t zbase = tmem + lane_addr + slot * Cfg::SLOT_COLS;
         const uint32_t abase = tmem + lane_addr + Cfg::ACC_COL;
-        // ---- before E1: the given flag and the fire decision, computed while GEMM1 runs.
-        const long long g = t * kTileM + m;
-        const bool valid = g < total;
+        // ---- before E1: index math, and the adaptive fire decision (it needs the fp32 state);
+        // the given flag and the other fire rules come from the stencil warps (s_flags).
+        const unsigned g = (unsigned)t * kTileM + m;
+        const bool valid = (long long)g < total;
         int inst = 0, p = 0, row = 0;
         if (valid) {
-          inst = (int)(g / A.HW);
-          p = (int)(g - (long long)inst * A.HW);
-          row = A.inst_row ? A.inst_row[inst] : inst / A.K;
+          inst = (int)fdiv(g, A.div_hw);
+          p = (int)(g - (unsigned)inst * A.HW);
+          row = A.inst_row ? A.inst_row[inst] : (int)fdiv((unsigned)inst, A.div_k);
         }
-        const bool gv = valid && A.given[(long long)row * A.HW + p] != 0;
-        // fire decision (needs the old state for the adaptive rule)
-        float f = 0.f;
-        if (valid) {
-          if (A.fire_mode == 0) {
-            f = A.masks[((long long)s * A.n_inst + inst) * A.HW + p] ? 1.f : 0.f;
-          } else {
-            float prob = A.p_fire;
-            if (A.fire_mode >= 2) {
-              float xo_[16];
-              for (int c = 0; c < A.c_out; ++c) {
-                const int cc = A.out_off + c;
-                xo_[c] = xin[(((t * (Cfg::C / 4) + (cc >> 2)) << 7) + m) * 4 + (cc & 3)];
-              }
-              float sc[16];
-              float mx = -3.402823466e38f;
-              for (int o = 0; o < A.n_out; ++o) {
-                float a = A.head_b[o];
-                for (int c = 0; c < A.c_out; ++c) a = fmaf(A.head_w[o][c], xo_[c], a);
-                sc[o] = a;
-                mx = fmaxf(mx, a);
-              }
-              float den = 0.f;
-              for (int o = 0; o < A.n_out; ++o) den += expf(sc[o] - mx);
-              float conf = fminf(fmaxf(1.f / den, 0.f), 1.f);
-              prob = A.ad_scale * (1.f - conf) + A.ad_bias;
-            }
-            float uu;
-            if (A.fire_mode == 3) uu = A.uniforms[((long long)s * A.n_inst + inst) * A.HW + p];
-            else uu = philox_uniform(A.seed, A.inst_offset + inst, p, step);
-            f = (uu < prob) ? 1.f : 0.f;
+        constexpr int NQ = CH / 4;  // float4 chunks of this thread
+        const float4* xin4 = reinterpret_cast<const float4*>(xin) + ((t * (Cfg::C / 4) + half * NQ) << 7) + m;
+        float f_adapt = 0.f;
+        if (valid && A.fire_mode >= 2) {
+          float xo_[16];
+          for (int c = 0; c < A.c_out; ++c) {
+            const int cc = A.out_off + c;
+            xo_[c] = xin[(((t * (Cfg::C / 4) + (cc >> 2)) << 7) + m) * 4 + (cc & 3)];
           }
+          float sc[16];
+          float mx = -3.402823466e38f;
+          for (int o = 0; o < A.n_out; ++o) {
+            float a = A.head_b[o];
+            for (int c = 0; c < A.c_out; ++c) a = fmaf(A.head_w[o][c], xo_[c], a);
+            sc[o] = a;
+            mx = fmaxf(mx, a);
+          }
+          float den = 0.f;
+          for (int o = 0; o < A.n_out; ++o) den += expf(sc[o] - mx);
+          const float conf = fminf(fmaxf(1.f / den, 0.f), 1.f);
+          const float prob = A.ad_scale * (1.f - conf) + A.ad_bias;
+          const float uu = A.fire_mode == 3 ? A.uniforms[((long long)s * A.n_inst + inst) * A.HW + p]
+                                            : philox_uniform(A.seed, A.inst_offset + inst, p, step);
+          f_adapt = (uu < prob) ? 1.f : 0.f;
         }
         // ---- E1: hidden = relu(acc1 + b1) -> bf16 into the z slot
         if (!warp_wait(&bars[half == 0 ? BAR_ACC_FULL : BAR_ACC_FULL_B], (uint32_t)it & 1, fs, W_E1_ACC)) { ok = false; break; }
@@ -645,7 +681,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           const int col = half * (Cfg::HD / 2) + cbk;
           uint32_t r[32];
           tmem_ld32(abase + col, r);
-          tc_wait_ld();
+          tc_wait_ld_regs(r);
           const float4* bb = reinterpret_cast<const float4*>(s_b1 + col);
           uint32_t hi[16];
           if constexpr (!Cfg::SPLIT) {
@@ -674,15 +710,17 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[half == 0 ? BAR_H_FULL : BAR_H_FULL_B]);
+        if (lane == 0) mbar_arrive_relaxed(&bars[half == 0 ? BAR_H_FULL : BAR_H_FULL_B]);
 
         // ---- E2: dx = acc2 + b2; x' = x + f * dx; clamp; store.  The old state of this thread's
-        // channels is loaded while GEMM2 runs (the loader prefetched the tile into L2).
-        constexpr int NQ = CH / 4;  // float4 chunks of this thread
+        // channels is loaded while GEMM2 runs.
         float4 xo[NQ];
-        const float4* xin4 = reinterpret_cast<const float4*>(xin) + ((t * (Cfg::C / 4) + half * NQ) << 7) + m;
 #pragma unroll
         for (int q = 0; q < NQ; ++q) xo[q] = valid ? __ldg(xin4 + (q << 7)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (!warp_wait(&bars[BAR_FLAGS + (it & 3)], (uint32_t)(it >> 2) & 1, fs, W_E2_FLAGS)) { ok = false; break; }
+        const uint32_t fl = s_flags[(it & 3) * kTileM + m];
+        const bool gv = (fl & 2u) != 0;
+        const float f = A.fire_mode >= 2 ? f_adapt : ((fl & 1u) ? 1.f : 0.f);
         if (!warp_wait(&bars[BAR_ACC2_FULL], (uint32_t)it & 1, fs, W_E2_ACC2)) { ok = false; break; }
         tc_fence_after();
         uint32_t r[CH];
@@ -691,15 +729,24 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         } else {
           tmem_ld16(abase + (Cfg::ACC2_COL - Cfg::ACC_COL) + half * CH, *reinterpret_cast<uint32_t(*)[16]>(r));
         }
-        tc_wait_ld();
+        tc_wait_ld_regs(r);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[BAR_ACC_EMPTY]);
+        if (lane == 0) mbar_arrive_relaxed(&bars[BAR_ACC_EMPTY]);
         if (valid) {
-          const float* clamp_row = A.clamp + ((long long)row * A.HW + p) * A.c_in;
           const float4* bb = reinterpret_cast<const float4*>(s_b2 + half * CH);
           const float2 ff = f2(f, f);
           float4* xout4 = reinterpret_cast<float4*>(xout) + ((t * (Cfg::C / 4) + half * NQ) << 7) + m;
+          // Clamp (src/nca/model.py:430-438) of the input slice of given cells.  The state this
+          // kernel reads is clamped already (the initial state is, and every step writes the
+          // clamp values back), so the old values of those channels are kept: a select per
+          // channel, no branch, no reads of the clamp rows.  A launch's first step also accepts
+          // an unclamped state and fixes the slice below.
+          const int lo_c = A.in_off - half * CH;  // input slice relative to this thread's channels
+          const unsigned long long slice = A.c_in >= 64 ? ~0ull : ((1ull << A.c_in) - 1ull);
+          const uint32_t keep = (gv && lo_c < CH && lo_c + A.c_in > 0)
+                                    ? (uint32_t)((slice << (lo_c + 32)) >> 32)
+                                    : 0u;
           uint32_t pk[CH / 2];
 #pragma unroll
           for (int q = 0; q < NQ; ++q) {
@@ -708,17 +755,10 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
             const float2 d1 = __fadd2_rn(f2(__uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])), f2(b.z, b.w));
             float2 y0 = __ffma2_rn(ff, d0, f2(xo[q].x, xo[q].y));
             float2 y1 = __ffma2_rn(ff, d1, f2(xo[q].z, xo[q].w));
-            const int c0_ = half * CH + 4 * q;  // first channel of this chunk
-            if (gv && c0_ + 4 > A.in_off && c0_ < A.in_off + A.c_in) {
-              float y[4] = {y0.x, y0.y, y1.x, y1.y};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int ci = c0_ + e - A.in_off;
-                if (ci >= 0 && ci < A.c_in) y[e] = clamp_row[ci];
-              }
-              y0 = f2(y[0], y[1]);
-              y1 = f2(y[2], y[3]);
-            }
+            y0.x = (keep >> (4 * q + 0)) & 1u ? xo[q].x : y0.x;
+            y0.y = (keep >> (4 * q + 1)) & 1u ? xo[q].y : y0.y;
+            y1.x = (keep >> (4 * q + 2)) & 1u ? xo[q].z : y1.x;
+            y1.y = (keep >> (4 * q + 3)) & 1u ? xo[q].w : y1.y;
             xout4[q << 7] = make_float4(y0.x, y0.y, y1.x, y1.y);
             pk[2 * q] = pack_bf16(y0.x, y0.y);
             pk[2 * q + 1] = pack_bf16(y1.x, y1.y);
@@ -728,6 +768,21 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
 #pragma unroll
             for (int q = 0; q < CH / 8; ++q)
               mout4[q << 7] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          }
+          if (s == 0 && keep != 0u) {
+            // first step of the launch: write the clamp values themselves over the kept slice
+            const float* clamp_row = A.clamp + ((long long)row * A.HW + p) * A.c_in;
+            float* xo1 = reinterpret_cast<float*>(xout4);
+            for (int j = 0; j < CH; ++j) {
+              if (!((keep >> j) & 1u)) continue;
+              const float v = clamp_row[half * CH + j - A.in_off];
+              xo1[((j >> 2) << 9) + (j & 3)] = v;  // float4 chunk j/4 is 128 rows (512 floats) apart
+              if constexpr (Cfg::SRC_BF16) {
+                __nv_bfloat16* mo = reinterpret_cast<__nv_bfloat16*>(mout) +
+                                    ((((t * (Cfg::C / 8) + half * (CH / 8) + (j >> 3)) << 7) + m) << 3) + (j & 7);
+                *mo = __float2bfloat16_rn(v);
+              }
+            }
           }
         }
         if (half == 0 && A.updates != nullptr) {

@@ -294,7 +294,7 @@ def run_ours(args) -> None:
                          "traffic": None if tb is None else tb * avg_cells,
                          "kernel": "nca_step_kernel", "flop_per_cell_update": flop_per_cu},
             "e2e": None if e2e_value is None else {
-                "value": e2e_value * world, "unit": UNIT, "h2d_bytes_per_step": h2d * world,
+                "value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d * world,
                 "d2h_bytes_per_step": d2h * world},
             "gpu_launches": launches,
             "clocks": clk.summary(),

@@ -413,11 +413,13 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         if (lane == 0) mbar_arrive_expect_tx(&bars[BAR_WIN_FULL + stage], (uint32_t)(NCH * (hi - lo) * 16));
         __syncwarp();
         const uint32_t dst = smem_u32(smem + L.win + stage * WC * Cfg::ROWB);
-        // one bulk copy per (chunk, tile overlapped by the window): at most 3 tiles
+        // one bulk copy per (chunk, tile overlapped by the window): 3 tiles while the board is
+        // narrower than a tile, up to 2 + ceil((2W + 2) / 128) for wider boards
         const long long t0 = lo >> 7;
-        for (int job = lane; job < NCH * 3; job += 32) {
-          const int ch = job / 3;
-          const long long T = t0 + job % 3;
+        const int nt = (int)(((hi - 1) >> 7) - t0 + 1);
+        for (int job = lane; job < NCH * nt; job += 32) {
+          const int ch = job / nt;
+          const long long T = t0 + job % nt;
           const long long c_lo = (T << 7) > lo ? (T << 7) : lo;
           const long long c_hi = ((T + 1) << 7) < hi ? ((T + 1) << 7) : hi;
           if (c_hi > c_lo) {

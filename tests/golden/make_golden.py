@@ -2,7 +2,7 @@
 
 Run in a container where the reference is importable (it is not on the GPU box):
 
-    PYTHONPATH=/path/to/reference/src python tests/golden/make_golden.py [/path/to/reference]
+    PYTHONPATH=/path/to/reference/src python tests/golden/make_golden.py /path/to/reference
 
 Every array in the file is produced by the reference's own code: nca.model.NCA (built through
 nca.model.build_model with the benchmark overrides and the benchmark's synthetic weights loaded
@@ -19,7 +19,9 @@ import numpy as np
 import torch
 
 REPO = Path(__file__).resolve().parents[2]
-REF = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+if len(sys.argv) < 2:
+    raise SystemExit("usage: python tests/golden/make_golden.py <reference checkout>")
+REF = Path(sys.argv[1])
 sys.path.insert(0, str(REF / "src"))
 sys.path.insert(0, str(REPO))
 

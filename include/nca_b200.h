@@ -95,6 +95,9 @@ typedef struct NcaState {
   float* master[2];         /* device, tiled fp32 */
   uint16_t* mirror[2];      /* device, tiled bf16 (NULL in NCA_PREC_SPLIT) */
   int32_t cur;              /* index of the buffers holding the current state */
+  int32_t clamped;          /* 1 when the given cells of the current state hold their clamp
+                               values (set by nca_b200_state_init and by every step; cleared by
+                               nca_b200_state_bind and nca_b200_state_load_nchw) */
 } NcaState;
 
 typedef struct NcaFireDesc {

@@ -76,6 +76,7 @@ class NcaState(C.Structure):
         ("master", C.c_void_p * 2),
         ("mirror", C.c_void_p * 2),
         ("cur", C.c_int32),
+        ("clamped", C.c_int32),
     ]
 
 
@@ -171,7 +172,7 @@ def lib() -> C.CDLL:
     global _lib
     if _lib is not None:
         return _lib
-    path = Path(os.environ.get("NCA_B200_LIB", LIB_PATH))
+    path = Path(os.environ.get("NCA_B200_LIB") or LIB_PATH)
     if not path.exists():
         raise RuntimeError(
             f"{path} is missing: build it with `python -c 'import __graft_entry__ as g; g.build()'`"

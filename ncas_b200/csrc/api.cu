@@ -57,6 +57,29 @@ __device__ __forceinline__ float clamp_value(const NcaBatchDesc& b, int c_in, in
   return v;
 }
 
+// The clamp of src/nca/model.py:430-438 on the current state: one thread per cell writes the
+// clamp values over the input slice of the given cells (fp32 state and bf16 mirror).  Run after
+// the first step on a state that was not clamped (loaded from outside the library); the step
+// kernel itself keeps the slice of given cells as it finds it.
+__global__ void clamp_fix_kernel(float* master, uint16_t* mirror, int C, long long total, int hw,
+                                 NcaBatchDesc b, int c_in, int in_off) {
+  const long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= total) return;
+  const int inst = (int)(g / hw);
+  const int p = (int)(g - (long long)inst * hw);
+  const int row = b.inst_row ? b.inst_row[inst] : inst / b.trials;
+  if (!b.given[(long long)row * hw + p]) return;
+  const long long t = g >> 7;
+  const int m = (int)(g & 127);
+  for (int ci = 0; ci < c_in; ++ci) {
+    const int c = in_off + ci;
+    const float v = b.clamp[((long long)row * hw + p) * c_in + ci];
+    master[((t * (C / 4) + (c >> 2)) * kTileM + m) * 4 + (c & 3)] = v;
+    if (mirror)
+      mirror[((t * (C / 8) + (c >> 3)) * kTileM + m) * 8 + (c & 7)] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  }
+}
+
 // One thread per (tile, 8-channel group, row): writes 8 channels of one cell.
 // mode 0: zero state + clamp; mode 1: load from NCHW.
 __global__ void state_fill_kernel(float* master, uint16_t* mirror, int C, long long n_tiles,
@@ -514,6 +537,7 @@ int32_t nca_b200_state_bind(NcaState* st, void* buffer, size_t bytes, int32_t n_
   st->mirror[0] = mirror ? reinterpret_cast<uint16_t*>(p + 2 * master) : nullptr;
   st->mirror[1] = mirror ? reinterpret_cast<uint16_t*>(p + 2 * master + mirror) : nullptr;
   st->cur = 0;
+  st->clamped = 0;
   return NCA_OK;
 }
 
@@ -526,6 +550,7 @@ int32_t nca_b200_state_init(NcaState* st, const NcaModelDesc* m, const NcaBatchD
   state_fill_kernel<<<(unsigned)((n + bs - 1) / bs), bs, 0, as_stream(stream)>>>(
       st->master[st->cur], st->mirror[st->cur], st->channels, st->n_tiles,
       (long long)st->n_inst * st->hw, st->hw, *b, m->c_in, m->in_offset, nullptr, 0);
+  st->clamped = 1;
   return cuda_status(cudaGetLastError());
 }
 
@@ -539,6 +564,7 @@ int32_t nca_b200_state_load_nchw(NcaState* st, const float* x_nchw, void* stream
   state_fill_kernel<<<(unsigned)((n + bs - 1) / bs), bs, 0, as_stream(stream)>>>(
       st->master[st->cur], st->mirror[st->cur], st->channels, st->n_tiles,
       (long long)st->n_inst * st->hw, st->hw, dummy, 0, 0, x_nchw, 1);
+  st->clamped = 0;
   return cuda_status(cudaGetLastError());
 }
 
@@ -564,15 +590,33 @@ int32_t nca_b200_run_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaStat
   const bool split = st->precision == NCA_PREC_SPLIT;
   cudaStream_t s = as_stream(stream);
   const int C = m->channels, HD = m->hidden;
-  if (C == 32 && HD == 128) {
-    return split ? launch_steps<StepCfg<32, 128, true>>(m, b, st, n_steps, fire, ctrl, timeout_ms, s)
-                 : launch_steps<StepCfg<32, 128, false>>(m, b, st, n_steps, fire, ctrl, timeout_ms, s);
-  }
-  if (C == 64 && HD == 256) {
-    return split ? launch_steps<StepCfg<64, 256, true>>(m, b, st, n_steps, fire, ctrl, timeout_ms, s)
-                 : launch_steps<StepCfg<64, 256, false>>(m, b, st, n_steps, fire, ctrl, timeout_ms, s);
-  }
-  return NCA_ERR_UNSUPPORTED;
+  auto launch = [&](int32_t n, const NcaFireDesc* f) -> int32_t {
+    if (C == 32 && HD == 128)
+      return split ? launch_steps<StepCfg<32, 128, true>>(m, b, st, n, f, ctrl, timeout_ms, s)
+                   : launch_steps<StepCfg<32, 128, false>>(m, b, st, n, f, ctrl, timeout_ms, s);
+    if (C == 64 && HD == 256)
+      return split ? launch_steps<StepCfg<64, 256, true>>(m, b, st, n, f, ctrl, timeout_ms, s)
+                   : launch_steps<StepCfg<64, 256, false>>(m, b, st, n, f, ctrl, timeout_ms, s);
+    return NCA_ERR_UNSUPPORTED;
+  };
+  if (st->clamped) return launch(n_steps, fire);
+  // A state from outside the library: the first step runs alone and is followed by the clamp
+  // of its output, as the reference clamps after every step; the remaining steps continue.
+  int32_t r = launch(1, fire);
+  if (r != NCA_OK) return r;
+  const long long total = (long long)st->n_inst * st->hw;
+  clamp_fix_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(
+      st->master[st->cur], st->mirror[st->cur], st->channels, total, st->hw, *b, m->c_in,
+      m->in_offset);
+  r = cuda_status(cudaGetLastError());
+  if (r != NCA_OK) return r;
+  st->clamped = 1;
+  if (n_steps == 1) return NCA_OK;
+  NcaFireDesc rest = *fire;
+  rest.step0 += 1;
+  if (rest.masks) rest.masks += total;
+  if (rest.uniforms) rest.uniforms += total;
+  return launch(n_steps - 1, &rest);
 }
 
 int32_t nca_b200_readout(const NcaModelDesc* m, const NcaBatchDesc* b, const NcaState* st,

@@ -14,9 +14,9 @@
 //                  E2: dx = acc2 + b2, fire mask, x' = x + f*dx, clamp, store (src/nca/model.py:
 //                  527-559, 430-438)
 //
-// Tensor memory (512 columns x 128 lanes): NZ slots holding z (then h) and one accumulator
-// region holding acc1 (then acc2 in its first C columns).  Every wait is bounded; a wait that
-// runs out records NCA_ERR_TIMEOUT in the control words and the CTA drains and exits.
+// Tensor memory (512 columns x 128 lanes): NZ slots holding z and one accumulator region
+// holding acc1, then h (bf16, over the columns already read) and acc2.  Every wait is bounded; a
+// wait that runs out records NCA_ERR_TIMEOUT in the control words and the CTA drains and exits.
 #pragma once
 #include <cuda_bf16.h>
 
@@ -216,6 +216,48 @@ __device__ __forceinline__ void fixed_taps4(float a, float b, float c, float d, 
   s = fmaf(2.f, f, s);
   s = fmaf(-12.f, e, s);
   lap = s * 0.0625f;
+}
+
+// Adaptive firing of one cell at step s (continuous rule on the reference's confidence,
+// src/nca/model.py:584-593, 624-629): conf = max softmax of the head scores of the cell's fp32
+// state, p = scale * (1 - conf) + bias, fire when u < p with u from Philox or from the caller.
+// Read from the fp32 state of the step's input buffer (complete since the last grid barrier).
+// The loops run to the compile-time maximum with uniform exits, so the slice stays in registers.
+template <class Cfg>
+__device__ __forceinline__ bool adaptive_fire(const StepArgs& A, int s, long long t, int m, int inst,
+                                              int p) {
+  const float* xin = A.master[(A.cur + s) & 1];
+  float xs[16];
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    xs[c] = 0.f;
+    if (c < A.c_out) {
+      const int cc = A.out_off + c;
+      xs[c] = __ldg(xin + ((((t * (Cfg::C / 4) + (cc >> 2)) << 7) + m) * 4 + (cc & 3)));
+    }
+  }
+  // two passes over the head (max, then the softmax denominator) recompute the scores instead
+  // of keeping them
+  auto score = [&](int o) {
+    float a = A.head_b[o];
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+      if (c < A.c_out) a = fmaf(A.head_w[o][c], xs[c], a);
+    return a;
+  };
+  float mx = -3.402823466e38f;
+#pragma unroll
+  for (int o = 0; o < 16; ++o)
+    if (o < A.n_out) mx = fmaxf(mx, score(o));
+  float den = 0.f;
+#pragma unroll
+  for (int o = 0; o < 16; ++o)
+    if (o < A.n_out) den += expf(score(o) - mx);
+  const float conf = fminf(fmaxf(1.f / den, 0.f), 1.f);
+  const float prob = A.ad_scale * (1.f - conf) + A.ad_bias;
+  const float u = A.fire_mode == 3 ? A.uniforms[((long long)s * A.n_inst + inst) * A.HW + p]
+                                   : philox_uniform(A.seed, A.inst_offset + inst, p, A.step0 + s);
+  return u < prob;
 }
 
 template <class Cfg>
@@ -472,16 +514,16 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           i = (int)fdiv((unsigned)p, A.div_w);
           j = p - i * W;
         }
-        if (half == 0) {
-          // per-row side information for the epilogue: given flag and (except for the adaptive
-          // rules, which need the fp32 state) the fire decision of this step
+        if (half == 0 && A.fire_mode < 2) {
+          // per-row side information for the epilogue: bit 0 the fire decision of this step,
+          // bit 1 given, bit 2 valid (the adaptive rules are evaluated after z, below)
           uint32_t fl = 0;
           if (valid) {
             const int row = A.inst_row ? A.inst_row[inst] : (int)fdiv((unsigned)inst, A.div_k);
             fl = 4u | (A.given[(long long)row * A.HW + p] ? 2u : 0u);
             if (A.fire_mode == 0) {
               fl |= A.masks[((long long)s * A.n_inst + inst) * A.HW + p] ? 1u : 0u;
-            } else if (A.fire_mode == 1) {
+            } else {
               fl |= philox_uniform(A.seed, A.inst_offset + inst, p, A.step0 + s) < A.p_fire ? 1u : 0u;
             }
           }
@@ -617,6 +659,19 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           mbar_arrive_relaxed(&bars[BAR_Z_FULL + slot]);
           mbar_arrive_relaxed(&bars[BAR_WIN_EMPTY + stage]);
         }
+        if (half == 0 && A.fire_mode >= 2) {
+          // adaptive rules: the fire decision needs the confidence of the cell's fp32 state; it
+          // is evaluated after z is handed to the MMA warp (the epilogue needs it a tile later)
+          uint32_t fl = 0;
+          if (valid) {
+            const int row = A.inst_row ? A.inst_row[inst] : (int)fdiv((unsigned)inst, A.div_k);
+            fl = 4u | (A.given[(long long)row * A.HW + p] ? 2u : 0u);
+            fl |= adaptive_fire<Cfg>(A, s, t, m, inst, p) ? 1u : 0u;
+          }
+          s_flags[(it & 3) * kTileM + m] = (uint8_t)fl;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars[BAR_FLAGS + (it & 3)]);
+        }
       }
     }
   } else if (!skip && warp >= kEpiWarp0) {
@@ -635,46 +690,18 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
       const float* xin = A.master[in];
       float* xout = A.master[out];
       uint16_t* mout = A.mirror[out];
-      const long long step = A.step0 + s;
       for (long long t = blockIdx.x; t < A.n_tiles; t += grid, ++it) {
         const int slot = (int)(it % Cfg::NZ);
         const uint32_t zbase = tmem + lane_addr + slot * Cfg::SLOT_COLS;
         const uint32_t abase = tmem + lane_addr + Cfg::ACC_COL;
-        // ---- before E1: index math, and the adaptive fire decision (it needs the fp32 state);
-        // the given flag and the other fire rules come from the stencil warps (s_flags).
+        // ---- before E1: index math; the fire and given flags come from the stencil warps
+        // (s_flags).
         const unsigned g = (unsigned)t * kTileM + m;
         const bool valid = (long long)g < total;
-        int inst = 0, p = 0, row = 0;
-        if (valid) {
-          inst = (int)fdiv(g, A.div_hw);
-          p = (int)(g - (unsigned)inst * A.HW);
-          row = A.inst_row ? A.inst_row[inst] : (int)fdiv((unsigned)inst, A.div_k);
-        }
+        int inst = 0;
+        if (valid) inst = (int)fdiv(g, A.div_hw);
         constexpr int NQ = CH / 4;  // float4 chunks of this thread
         const float4* xin4 = reinterpret_cast<const float4*>(xin) + ((t * (Cfg::C / 4) + half * NQ) << 7) + m;
-        float f_adapt = 0.f;
-        if (valid && A.fire_mode >= 2) {
-          float xo_[16];
-          for (int c = 0; c < A.c_out; ++c) {
-            const int cc = A.out_off + c;
-            xo_[c] = xin[(((t * (Cfg::C / 4) + (cc >> 2)) << 7) + m) * 4 + (cc & 3)];
-          }
-          float sc[16];
-          float mx = -3.402823466e38f;
-          for (int o = 0; o < A.n_out; ++o) {
-            float a = A.head_b[o];
-            for (int c = 0; c < A.c_out; ++c) a = fmaf(A.head_w[o][c], xo_[c], a);
-            sc[o] = a;
-            mx = fmaxf(mx, a);
-          }
-          float den = 0.f;
-          for (int o = 0; o < A.n_out; ++o) den += expf(sc[o] - mx);
-          const float conf = fminf(fmaxf(1.f / den, 0.f), 1.f);
-          const float prob = A.ad_scale * (1.f - conf) + A.ad_bias;
-          const float uu = A.fire_mode == 3 ? A.uniforms[((long long)s * A.n_inst + inst) * A.HW + p]
-                                            : philox_uniform(A.seed, A.inst_offset + inst, p, step);
-          f_adapt = (uu < prob) ? 1.f : 0.f;
-        }
         // ---- E1: hidden = relu(acc1 + b1) -> bf16 into the z slot
         if (!warp_wait(&bars[half == 0 ? BAR_ACC_FULL : BAR_ACC_FULL_B], (uint32_t)it & 1, fs, W_E1_ACC)) { ok = false; break; }
         tc_fence_after();
@@ -722,7 +749,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         if (!warp_wait(&bars[BAR_FLAGS + (it & 3)], (uint32_t)(it >> 2) & 1, fs, W_E2_FLAGS)) { ok = false; break; }
         const uint32_t fl = s_flags[(it & 3) * kTileM + m];
         const bool gv = (fl & 2u) != 0;
-        const float f = A.fire_mode >= 2 ? f_adapt : ((fl & 1u) ? 1.f : 0.f);
+        const float f = (fl & 1u) ? 1.f : 0.f;
         if (!warp_wait(&bars[BAR_ACC2_FULL], (uint32_t)it & 1, fs, W_E2_ACC2)) { ok = false; break; }
         tc_fence_after();
         uint32_t r[CH];
@@ -740,16 +767,19 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           const float2 ff = f2(f, f);
           float4* xout4 = reinterpret_cast<float4*>(xout) + ((t * (Cfg::C / 4) + half * NQ) << 7) + m;
           // Clamp (src/nca/model.py:430-438) of the input slice of given cells.  The state this
-          // kernel reads is clamped already (the initial state is, and every step writes the
-          // clamp values back), so the old values of those channels are kept: a select per
-          // channel, no branch, no reads of the clamp rows.  A launch's first step also accepts
-          // an unclamped state and fixes the slice below.
+          // kernel reads is clamped already (the initial state is, every step keeps it so, and
+          // the host follows the first step on an unclamped state with a clamp pass), so the old
+          // values of those channels are kept: a select per channel, no branch, no reads of the
+          // clamp rows.
           const int lo_c = A.in_off - half * CH;  // input slice relative to this thread's channels
           const unsigned long long slice = A.c_in >= 64 ? ~0ull : ((1ull << A.c_in) - 1ull);
           const uint32_t keep = (gv && lo_c < CH && lo_c + A.c_in > 0)
                                     ? (uint32_t)((slice << (lo_c + 32)) >> 32)
                                     : 0u;
-          uint32_t pk[CH / 2];
+          // the bf16 mirror of each 8 channels is stored as soon as they are done (fewer live
+          // registers than packing all of them first)
+          uint4* mout4 = reinterpret_cast<uint4*>(mout) + ((t * (Cfg::C / 8) + half * (CH / 8)) << 7) + m;
+          uint32_t pk[4];
 #pragma unroll
           for (int q = 0; q < NQ; ++q) {
             const float4 b = bb[q];
@@ -762,28 +792,10 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
             y1.x = (keep >> (4 * q + 2)) & 1u ? xo[q].z : y1.x;
             y1.y = (keep >> (4 * q + 3)) & 1u ? xo[q].w : y1.y;
             xout4[q << 7] = make_float4(y0.x, y0.y, y1.x, y1.y);
-            pk[2 * q] = pack_bf16(y0.x, y0.y);
-            pk[2 * q + 1] = pack_bf16(y1.x, y1.y);
-          }
-          if constexpr (Cfg::SRC_BF16) {
-            uint4* mout4 = reinterpret_cast<uint4*>(mout) + ((t * (Cfg::C / 8) + half * (CH / 8)) << 7) + m;
-#pragma unroll
-            for (int q = 0; q < CH / 8; ++q)
-              mout4[q << 7] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          }
-          if (s == 0 && keep != 0u) {
-            // first step of the launch: write the clamp values themselves over the kept slice
-            const float* clamp_row = A.clamp + ((long long)row * A.HW + p) * A.c_in;
-            float* xo1 = reinterpret_cast<float*>(xout4);
-            for (int j = 0; j < CH; ++j) {
-              if (!((keep >> j) & 1u)) continue;
-              const float v = clamp_row[half * CH + j - A.in_off];
-              xo1[((j >> 2) << 9) + (j & 3)] = v;  // float4 chunk j/4 is 128 rows (512 floats) apart
-              if constexpr (Cfg::SRC_BF16) {
-                __nv_bfloat16* mo = reinterpret_cast<__nv_bfloat16*>(mout) +
-                                    ((((t * (Cfg::C / 8) + half * (CH / 8) + (j >> 3)) << 7) + m) << 3) + (j & 7);
-                *mo = __float2bfloat16_rn(v);
-              }
+            if constexpr (Cfg::SRC_BF16) {
+              pk[2 * (q & 1)] = pack_bf16(y0.x, y0.y);
+              pk[2 * (q & 1) + 1] = pack_bf16(y1.x, y1.y);
+              if (q & 1) mout4[(q >> 1) << 7] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
           }
         }

@@ -266,3 +266,30 @@ def test_invalid_batch_raises():
     eng = m.engine()
     with pytest.raises(L.NcaError):
         eng.new_state(0, 361)
+
+
+def test_unclamped_input_state_is_clamped_after_the_first_step():
+    """A state loaded from outside the library (not clamped) is stepped with the reference's
+    semantics: perception sees the unclamped values, the clamp follows every step
+    (src/nca/model.py:503-525, 430-438)."""
+    boards = sudoku_boards(4, seed=21)
+    K, D = 2, 3
+    m = build("sudoku", seed=0, device=DEV, precision="split")
+    eng = m.engine()
+    B = 4 * K
+    b = eng.batch_from_boards(boards.inputs, boards.given, K)
+    x = torch.randn((B, 64, 81), generator=torch.Generator().manual_seed(3)).to(DEV) * 0.5
+    st = eng.new_state(B, 81)
+    eng.load_nchw(st, x)
+    masks = (np.random.default_rng(8).random((D, B, 81)) < 0.5).astype(np.uint8)
+    eng.run(st, b, D, mode="mask", masks=torch.from_numpy(masks).to(DEV))
+    got = eng.store_nchw(st).reshape(B, 64, 9, 9).cpu().numpy()
+    eng.check()
+    p, _ = oracle_params("sudoku")
+    inputs_k = np.repeat(boards.inputs, K, 0)
+    given_k = np.repeat(boards.given, K, 0)
+    _, g4, clamp = O.init_state(inputs_k, given_k, p, 64)
+    ref = x.reshape(B, 64, 9, 9).cpu().numpy()
+    for t in range(D):
+        ref = O.step(ref, g4, clamp, masks[t].reshape(B, 1, 9, 9).astype(np.float32), p)
+    assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max()

@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define NCA_B200_ABI_VERSION 1
+#define NCA_B200_ABI_VERSION 2
 #define NCA_B200_MAX_OUT 16   /* maximum number of readout tokens (n_out) and readout channels */
 
 typedef enum NcaStatus {
@@ -86,7 +86,11 @@ typedef struct NcaBatchDesc {
   const uint8_t* given;     /* device [rows][H*W] 1 = clamped cell (given4) */
   const float* clamp;       /* device [rows][H*W][c_in] clamp values (embedding of the input) */
   const uint8_t* inputs;    /* device [rows][H*W] input tokens (readout fills given cells) */
-  const int32_t* inst_row;  /* optional device [n_inst] */
+  const int32_t* inst_row;  /* optional device [n_inst]: board row of each instance (default
+                               instance / trials) */
+  const int32_t* inst_id;   /* optional device [n_inst]: trial identity of each instance for the
+                               Philox counters (default the instance index), so a trial keeps its
+                               random stream when a compacted batch renumbers it */
 } NcaBatchDesc;
 
 typedef struct NcaState {
@@ -182,6 +186,28 @@ int32_t nca_b200_prune_refill(const uint8_t* pred, const float* board_conf, int3
  * x[sel] of src/nca/rollout.py:270-274, without compaction).  In place: every source must map to
  * itself (src[src[i]] == src[i]), as the maps written by nca_b200_prune_refill do. */
 int32_t nca_b200_clone(NcaState* st, const int32_t* src, void* stream);
+
+/* Niche-Capped Diversity Pruning, halving variant (src/nca/pruning.py:22-65), in two calls
+ * around the host's random draws.  The alive trials of board n are the rows
+ * [row_start[n], row_start[n + 1]) of a compacted batch, in increasing trial order.
+ * nca_b200_niches groups them by identical decoded grid (pruning.py:39-41): niche[r] is the index
+ * of the niche of row r in order of first appearance, rank[r] its position in the niche by
+ * decreasing confidence (stable, pruning.py:43-46), n_niches[n] the board's niche count.
+ * The host then draws the niche order of every board with more than one alive trial
+ * (rng.permutation(n_niches[n]), pruning.py:48), concatenated in `order` from order_start[n].
+ * nca_b200_halving keeps floor(alive / 2) rows per board, taken round-robin over the niches in
+ * that order, most confident first, at most n_cap per niche (pruning.py:49-61): keep[r]. */
+int32_t nca_b200_niches(const uint8_t* pred, const float* board_conf, const int32_t* row_start,
+                        int32_t n_boards, int32_t max_rows, int32_t hw, int32_t* niche,
+                        int32_t* rank, int32_t* n_niches, void* stream);
+int32_t nca_b200_halving(const int32_t* niche, const int32_t* rank, const int32_t* n_niches,
+                         const int32_t* row_start, const int32_t* order,
+                         const int32_t* order_start, int32_t n_boards, int32_t max_rows,
+                         int32_t n_cap, uint8_t* keep, void* stream);
+/* Compaction of a batch (x[sel] of src/nca/rollout.py:262-274): instance i of dst receives the
+ * current state of instance sel[i] of src, for i < dst->n_inst.  Both states have the same
+ * channels, cells and precision; dst is a separate workspace. */
+int32_t nca_b200_gather(const NcaState* src, NcaState* dst, const int32_t* sel, void* stream);
 
 /* ---- control words ------------------------------------------------------------------------ */
 /* Synchronises `stream`, reads the control words and returns NCA_OK or the first kernel-side

@@ -15,6 +15,7 @@ LIB_DIR = Path(__file__).resolve().parent / "_lib"
 LIB_PATH = LIB_DIR / "libnca_b200.so"
 
 MAX_OUT = 16
+ABI_VERSION = 2  # NCA_B200_ABI_VERSION of include/nca_b200.h
 
 NCA_OK = 0
 STATUS_NAMES = {
@@ -63,6 +64,7 @@ class NcaBatchDesc(C.Structure):
         ("clamp", C.c_void_p),
         ("inputs", C.c_void_p),
         ("inst_row", C.c_void_p),
+        ("inst_id", C.c_void_p),
     ]
 
 
@@ -142,6 +144,9 @@ SIGNATURES = {
     "nca_b200_select": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _I, _P, _P]),
     "nca_b200_prune_refill": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P]),
     "nca_b200_clone": (_I, [C.POINTER(NcaState), _P, _P]),
+    "nca_b200_niches": (_I, [_P, _P, _P, _I, _I, _I, _P, _P, _P, _P]),
+    "nca_b200_halving": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _P]),
+    "nca_b200_gather": (_I, [C.POINTER(NcaState), C.POINTER(NcaState), _P, _P]),
     "nca_b200_ctrl_status": (_I, [_P, C.POINTER(_I), _P]),
     "nca_b200_selftest_timeout": (_I, [_P, _I, _P]),
     "nca_b200_run_steps_static": (

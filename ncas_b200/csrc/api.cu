@@ -301,6 +301,124 @@ __global__ void prune_refill_kernel(const uint8_t* pred, const float* conf, int 
   }
 }
 
+// Niches of the halving rule (src/nca/pruning.py:39-46), one block per board: the board's alive
+// trials are the rows [row_start[b], row_start[b + 1]) (increasing trial order).  niche[r] is the
+// index of r's niche in order of first appearance, rank[r] its position in the niche by
+// decreasing confidence, ties by row (Python's stable sort on -conf).
+__global__ void niche_kernel(const uint8_t* pred, const float* conf, const int* row_start, int hw,
+                             int max_rows, int* niche, int* rank, int* n_niches) {
+  extern __shared__ uint8_t sm[];
+  const int b = blockIdx.x;
+  const int r0 = row_start[b], nr = row_start[b + 1] - r0;
+  if (nr < 0 || nr > max_rows) return;  // inconsistent row_start: leave the outputs untouched
+  uint64_t* hsh = reinterpret_cast<uint64_t*>(sm);
+  float* cf = reinterpret_cast<float*>(hsh + nr);
+  int* first = reinterpret_cast<int*>(cf + nr);   // first row (local) with the same grid
+  int* nid = first + nr;                          // niche index of the row
+  for (int i = threadIdx.x; i < nr; i += blockDim.x) {
+    hsh[i] = fnv1a64(pred + (long long)(r0 + i) * hw, hw);
+    cf[i] = conf[r0 + i];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < nr; i += blockDim.x) {
+    int f = i;
+    for (int j = 0; j < i; ++j) {
+      if (hsh[j] != hsh[i]) continue;
+      const uint8_t* a = pred + (long long)(r0 + j) * hw;
+      const uint8_t* c = pred + (long long)(r0 + i) * hw;
+      bool eq = true;
+      for (int p = 0; p < hw; ++p)
+        if (a[p] != c[p]) { eq = false; break; }
+      if (eq) { f = j; break; }
+    }
+    first[i] = f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < nr; i += blockDim.x) {
+    int idx = 0;  // niches that appear before this row's niche
+    for (int j = 0; j < first[i]; ++j) idx += first[j] == j ? 1 : 0;
+    nid[i] = idx;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < nr; i += blockDim.x) {
+    int rk = 0;
+    for (int j = 0; j < nr; ++j)
+      if (nid[j] == nid[i] && (cf[j] > cf[i] || (cf[j] == cf[i] && j < i))) ++rk;
+    niche[r0 + i] = nid[i];
+    rank[r0 + i] = rk;
+  }
+  if (threadIdx.x == 0) {
+    int cnt = 0;
+    for (int j = 0; j < nr; ++j) cnt += first[j] == j ? 1 : 0;
+    n_niches[b] = cnt;
+  }
+}
+
+// Survivors of the halving (src/nca/pruning.py:47-61), one block per board.  The member of rank d
+// of niche j sits at position sum_j' min(len_j', d) + #{j' before j in the order: len_j' > d} of
+// the round-robin sequence (len = niche size capped at n_cap); the first floor(alive / 2)
+// positions survive.  Boards with at most one alive trial keep it.
+__global__ void halving_kernel(const int* niche, const int* rank, const int* n_niches,
+                               const int* row_start, const int* order, const int* order_start,
+                               int n_cap, int max_rows, uint8_t* keep) {
+  extern __shared__ int shm[];
+  const int b = blockIdx.x;
+  const int r0 = row_start[b], nr = row_start[b + 1] - r0;
+  const int nn = n_niches[b];
+  int* len = shm;         // capped niche sizes
+  int* pos = shm + nr;    // position of each niche in the drawn order
+  if (nr > max_rows || nn > nr) return;  // inconsistent arguments: leave keep untouched
+  if (nr <= 1) {
+    for (int i = threadIdx.x; i < nr; i += blockDim.x) keep[r0 + i] = 1;
+    return;
+  }
+  for (int j = threadIdx.x; j < nn; j += blockDim.x) {
+    len[j] = 0;
+    const int o = order[order_start[b] + j];
+    if (o >= 0 && o < nn) pos[o] = j;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < nr; i += blockDim.x)
+    if (rank[r0 + i] < n_cap) atomicAdd(&len[niche[r0 + i]], 1);
+  __syncthreads();
+  const int target = nr / 2;
+  for (int i = threadIdx.x; i < nr; i += blockDim.x) {
+    const int j = niche[r0 + i], d = rank[r0 + i];
+    bool k = false;
+    if (d < n_cap) {
+      int p = 0;
+      for (int q = 0; q < nn; ++q) {
+        p += len[q] < d ? len[q] : d;
+        if (pos[q] < pos[j] && len[q] > d) ++p;
+      }
+      k = p < target;
+    }
+    keep[r0 + i] = k ? 1 : 0;
+  }
+}
+
+// One thread per (destination instance, cell, 4-channel chunk): dst instance i <- src sel[i].
+__global__ void gather_kernel(const float* smaster, const uint16_t* smirror, float* dmaster,
+                              uint16_t* dmirror, int C, int hw, int n_dst, const int* sel) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int C4 = C / 4;
+  if (idx >= (long long)n_dst * hw * C4) return;
+  const int c4 = (int)(idx % C4);
+  const long long g = idx / C4;
+  const int i = (int)(g / hw);
+  const int p = (int)(g - (long long)i * hw);
+  const long long gs = (long long)sel[i] * hw + p;
+  const float4* src = reinterpret_cast<const float4*>(smaster) + ((gs >> 7) * C4 + c4) * kTileM + (gs & 127);
+  float4* dst = reinterpret_cast<float4*>(dmaster) + ((g >> 7) * C4 + c4) * kTileM + (g & 127);
+  *dst = *src;
+  if (smirror && (c4 & 1) == 0) {
+    const int c8 = c4 >> 1, C8 = C / 8;
+    const uint4* ms = reinterpret_cast<const uint4*>(smirror) + ((gs >> 7) * C8 + c8) * kTileM + (gs & 127);
+    uint4* md = reinterpret_cast<uint4*>(dmirror) + ((g >> 7) * C8 + c8) * kTileM + (g & 127);
+    *md = *ms;
+  }
+}
+
 // One thread per (instance, cell, 4-channel chunk) of the destination.
 __global__ void clone_kernel(float* master, uint16_t* mirror, int C, int hw, int n_inst,
                              const int* src) {
@@ -380,6 +498,7 @@ int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaState* st,
   A.given = b->given;
   A.clamp = b->clamp;
   A.inst_row = b->inst_row;
+  A.inst_id = b->inst_id;
   A.master[0] = st->master[0];
   A.master[1] = st->master[1];
   A.mirror[0] = st->mirror[0];
@@ -673,6 +792,51 @@ int32_t nca_b200_clone(NcaState* st, const int32_t* src, void* stream) {
   const int bs = 256;
   clone_kernel<<<(unsigned)((n + bs - 1) / bs), bs, 0, as_stream(stream)>>>(
       st->master[st->cur], st->mirror[st->cur], st->channels, st->hw, st->n_inst, src);
+  return cuda_status(cudaGetLastError());
+}
+
+int32_t nca_b200_niches(const uint8_t* pred, const float* board_conf, const int32_t* row_start,
+                        int32_t n_boards, int32_t max_rows, int32_t hw, int32_t* niche,
+                        int32_t* rank, int32_t* n_niches, void* stream) {
+  if (!pred || !board_conf || !row_start || !niche || !rank || !n_niches || n_boards <= 0 ||
+      max_rows <= 0 || hw <= 0)
+    return NCA_ERR_INVALID;
+  if (max_rows > 4096) return NCA_ERR_UNSUPPORTED;
+  const size_t sm = (size_t)max_rows * (8 + 4 + 4 + 4);
+  const int threads = max_rows < 1024 ? ((max_rows + 31) / 32) * 32 : 1024;
+  niche_kernel<<<n_boards, threads, sm, as_stream(stream)>>>(pred, board_conf, row_start, hw,
+                                                              max_rows, niche, rank, n_niches);
+  return cuda_status(cudaGetLastError());
+}
+
+int32_t nca_b200_halving(const int32_t* niche, const int32_t* rank, const int32_t* n_niches,
+                         const int32_t* row_start, const int32_t* order,
+                         const int32_t* order_start, int32_t n_boards, int32_t max_rows,
+                         int32_t n_cap, uint8_t* keep, void* stream) {
+  if (!niche || !rank || !n_niches || !row_start || !order || !order_start || !keep ||
+      n_boards <= 0 || max_rows <= 0 || n_cap < 1)
+    return NCA_ERR_INVALID;
+  if (max_rows > 4096) return NCA_ERR_UNSUPPORTED;
+  const size_t sm = (size_t)max_rows * 8;
+  const int threads = max_rows < 1024 ? ((max_rows + 31) / 32) * 32 : 1024;
+  halving_kernel<<<n_boards, threads, sm, as_stream(stream)>>>(niche, rank, n_niches, row_start,
+                                                                order, order_start, n_cap, max_rows, keep);
+  return cuda_status(cudaGetLastError());
+}
+
+int32_t nca_b200_gather(const NcaState* src, NcaState* dst, const int32_t* sel, void* stream) {
+  if (!src || !dst || !sel) return NCA_ERR_INVALID;
+  if (src->channels != dst->channels || src->hw != dst->hw || src->precision != dst->precision ||
+      dst->n_inst > src->n_inst)
+    return NCA_ERR_INVALID;
+  const long long n = (long long)dst->n_inst * dst->hw * (dst->channels / 4);
+  if (n > 0) {
+    const int bs = 256;
+    gather_kernel<<<(unsigned)((n + bs - 1) / bs), bs, 0, as_stream(stream)>>>(
+        src->master[src->cur], src->mirror[src->cur], dst->master[dst->cur], dst->mirror[dst->cur],
+        dst->channels, dst->hw, dst->n_inst, sel);
+  }
+  dst->clamped = src->clamped;
   return cuda_status(cudaGetLastError());
 }
 

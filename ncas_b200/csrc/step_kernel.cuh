@@ -101,6 +101,7 @@ struct StepArgs {
   const uint8_t* given;
   const float* clamp;
   const int* inst_row;
+  const int* inst_id;
   float* master[2];
   uint16_t* mirror[2];
   int cur;
@@ -256,7 +257,7 @@ __device__ __forceinline__ bool adaptive_fire(const StepArgs& A, int s, long lon
   const float conf = fminf(fmaxf(1.f / den, 0.f), 1.f);
   const float prob = A.ad_scale * (1.f - conf) + A.ad_bias;
   const float u = A.fire_mode == 3 ? A.uniforms[((long long)s * A.n_inst + inst) * A.HW + p]
-                                   : philox_uniform(A.seed, A.inst_offset + inst, p, A.step0 + s);
+                                   : philox_uniform(A.seed, A.inst_offset + (A.inst_id ? A.inst_id[inst] : inst), p, A.step0 + s);
   return u < prob;
 }
 
@@ -524,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
             if (A.fire_mode == 0) {
               fl |= A.masks[((long long)s * A.n_inst + inst) * A.HW + p] ? 1u : 0u;
             } else {
-              fl |= philox_uniform(A.seed, A.inst_offset + inst, p, A.step0 + s) < A.p_fire ? 1u : 0u;
+              fl |= philox_uniform(A.seed, A.inst_offset + (A.inst_id ? A.inst_id[inst] : inst), p, A.step0 + s) < A.p_fire ? 1u : 0u;
             }
           }
           s_flags[(it & 3) * kTileM + m] = (uint8_t)fl;

@@ -48,6 +48,7 @@ class Batch:
     clamp: torch.Tensor   # (rows, H*W, c_in) fp32
     inputs: torch.Tensor  # (rows, H*W) uint8
     inst_row: torch.Tensor | None
+    inst_id: torch.Tensor | None = None
 
     @property
     def hw(self) -> int:
@@ -143,9 +144,11 @@ class B200Engine:
         n_inst: int | None = None,
         inst_offset: int = 0,
         inst_row: torch.Tensor | None = None,
+        inst_id: torch.Tensor | None = None,
     ) -> Batch:
         """given (rows, H, W) bool/uint8, clamp (rows, H, W, c_in) fp32, inputs (rows, H, W)
-        tokens; instance i uses row inst_row[i] or i // trials."""
+        tokens; instance i uses row inst_row[i] or i // trials, and Philox counters of trial
+        inst_offset + inst_id[i] (default inst_offset + i)."""
         rows, H, W = given.shape
         dev = self.device
         g = given.to(dev, torch.uint8).reshape(rows, H * W).contiguous()
@@ -153,12 +156,28 @@ class B200Engine:
         x = inputs.to(dev, torch.uint8).reshape(rows, H * W).contiguous()
         n = rows * trials if n_inst is None else n_inst
         ir = None if inst_row is None else inst_row.to(dev, torch.int32).contiguous()
+        iid = None if inst_id is None else inst_id.to(dev, torch.int32).contiguous()
         d = L.NcaBatchDesc()
         d.n_inst, d.height, d.width, d.trials = n, H, W, trials
         d.inst_offset = int(inst_offset)
         d.given, d.clamp, d.inputs = g.data_ptr(), c.data_ptr(), x.data_ptr()
         d.inst_row = _ptr(ir)
-        return Batch(d, n, H, W, trials, g, c, x, ir)
+        d.inst_id = _ptr(iid)
+        return Batch(d, n, H, W, trials, g, c, x, ir, iid)
+
+    def compacted(self, b: Batch, sel: torch.Tensor) -> Batch:
+        """The batch of the instances `sel` (increasing) of b: same board rows and Philox trial
+        identities, renumbered 0 .. len(sel) - 1 (the compaction of src/nca/rollout.py:262-274)."""
+        dev = self.device
+        sel = sel.to(dev, torch.int64)
+        rows = b.inst_row.long() if b.inst_row is not None else torch.div(
+            torch.arange(b.n_inst, device=dev), b.trials, rounding_mode="floor")
+        ids = b.inst_id.long() if b.inst_id is not None else torch.arange(b.n_inst, device=dev)
+        g = b.given.reshape(-1, b.height, b.width)
+        cl = b.clamp.reshape(-1, b.height, b.width, self.cfg.c_in)
+        x = b.inputs.reshape(-1, b.height, b.width)
+        return self.make_batch(g, cl, x, b.trials, n_inst=int(sel.numel()),
+                               inst_offset=b.desc.inst_offset, inst_row=rows[sel], inst_id=ids[sel])
 
     def batch_from_boards(self, inputs_np: np.ndarray, given_np: np.ndarray, trials: int,
                           inst_offset: int = 0) -> Batch:
@@ -309,6 +328,67 @@ class B200Engine:
         L.check(L.lib().nca_b200_clone(C.byref(st.st), src.data_ptr(), self._s()), "nca_b200_clone")
         self.launches += 2
         return src, kept
+
+    def halving(self, pred: torch.Tensor, board_conf: torch.Tensor, rows_per_board: np.ndarray,
+                n_cap: int, rng: np.random.Generator) -> torch.Tensor:
+        """Niche-Capped Diversity Pruning, halving variant (src/nca/pruning.py:22-65), on the
+        alive rows of a compacted batch: board n owns rows_per_board[n] consecutive rows in
+        increasing trial order.  Niches and survivors are computed on the device; the host
+        draws rng.permutation(n_niches) for every board with more than one alive trial, in
+        board order, as the reference does.  Returns keep (rows,) uint8 on the device."""
+        dev = self.device
+        n = len(rows_per_board)
+        rows = int(pred.shape[0])
+        starts = np.zeros(n + 1, dtype=np.int32)
+        np.cumsum(rows_per_board, out=starts[1:])
+        if starts[-1] != rows:
+            raise ValueError("rows_per_board does not add up to the batch")
+        max_rows = max(1, int(np.max(rows_per_board)) if n else 1)
+        row_start = torch.from_numpy(starts).to(dev)
+        niche = torch.empty(rows, dtype=torch.int32, device=dev)
+        rank = torch.empty(rows, dtype=torch.int32, device=dev)
+        n_niches = torch.empty(n, dtype=torch.int32, device=dev)
+        hw = int(pred.shape[-1])
+        L.check(
+            L.lib().nca_b200_niches(
+                pred.data_ptr(), board_conf.data_ptr(), row_start.data_ptr(), n, max_rows, hw,
+                niche.data_ptr(), rank.data_ptr(), n_niches.data_ptr(), self._s()
+            ),
+            "nca_b200_niches",
+        )
+        nn = n_niches.cpu().numpy()
+        order = np.zeros(max(1, int(nn.sum())), dtype=np.int32)
+        order_start = np.zeros(n, dtype=np.int32)
+        pos = 0
+        for b in range(n):
+            order_start[b] = pos
+            if rows_per_board[b] > 1:
+                order[pos : pos + nn[b]] = rng.permutation(int(nn[b]))
+            else:
+                order[pos : pos + nn[b]] = np.arange(nn[b])
+            pos += int(nn[b])
+        keep = torch.empty(rows, dtype=torch.uint8, device=dev)
+        order_d = torch.from_numpy(order).to(dev)
+        order_start_d = torch.from_numpy(order_start).to(dev)
+        L.check(
+            L.lib().nca_b200_halving(
+                niche.data_ptr(), rank.data_ptr(), n_niches.data_ptr(), row_start.data_ptr(),
+                order_d.data_ptr(), order_start_d.data_ptr(), n, max_rows, int(n_cap),
+                keep.data_ptr(), self._s()
+            ),
+            "nca_b200_halving",
+        )
+        self.launches += 2
+        return keep
+
+    def gather(self, st: State, sel: torch.Tensor) -> State:
+        """A new state holding the instances `sel` of st (compaction)."""
+        sel32 = sel.to(self.device, torch.int32).contiguous()
+        dst = self.new_state(int(sel32.numel()), st.hw)
+        L.check(L.lib().nca_b200_gather(C.byref(st.st), C.byref(dst.st), sel32.data_ptr(), self._s()),
+                "nca_b200_gather")
+        self.launches += 1
+        return dst
 
     # ----------------------------------------------------------- reference-shaped NCHW calls
     def _nchw_batch(self, x: torch.Tensor, given4: torch.Tensor, clamp: torch.Tensor) -> Batch:

@@ -20,6 +20,14 @@ Rules beyond the reference's uniform firing:
   niche-capped pruning with refill: RolloutConfig.pruning = {"every": s, "n_cap": c}
       every s steps, per board: group trials by decoded grid, keep the c most confident per
       niche, refill the dropped slots with clones of the kept trials (K stays constant).
+
+The reference's pruning, RolloutConfig.pruning = {"m": m, "n_cap": c}, halves the alive trials
+of every board at m - 1 equidistant checkpoints (src/nca/pruning.py:22-65) and compacts the batch
+(src/nca/rollout.py:249-275): niches and survivors are computed on the device, the niche orders
+are drawn from numpy.random.default_rng(seed) in the reference's order, and the surviving
+states are gathered into a smaller state, so the steps after a checkpoint cost less.  A pruned
+trial keeps its last values (alive False), and its Philox stream does not change when the batch
+is renumbered.
 """
 
 from __future__ import annotations
@@ -99,9 +107,22 @@ def _check_config(rc) -> None:
     if getattr(rc, "damage_at", None) is not None:
         raise ValueError("damage events are not implemented by the b200 backend")
     pr = getattr(rc, "pruning", None)
-    if pr is not None and "every" not in pr:
-        raise ValueError("the b200 backend implements niche-capped pruning with refill "
-                         "(pruning={'every': s, 'n_cap': c})")
+    if pr is not None and "every" not in pr and "m" not in pr:
+        raise ValueError("pruning needs 'm' (halving at m - 1 checkpoints, src/nca/pruning.py) or "
+                         "'every' (niche-capped pruning with refill)")
+
+
+def _prune_steps(rc) -> tuple[str | None, set[int], int]:
+    """(mode, steps after which to prune, n_cap)."""
+    pr = rc.pruning
+    if not pr:
+        return None, set(), 0
+    if "m" in pr:  # the reference's checkpoints (src/nca/rollout.py:154-158)
+        m = int(pr["m"])
+        dt = rc.depth // m
+        return "halving", {i * dt for i in range(1, m)}, int(pr.get("n_cap", 3))
+    every = int(pr["every"])
+    return "refill", set(range(every, rc.depth, every)), int(pr.get("n_cap", 2))
 
 
 def rollout(model, task: Task, boards: Boards, rc, seed: int = 0, task_ids=None,
@@ -128,21 +149,23 @@ def rollout(model, task: Task, boards: Boards, rc, seed: int = 0, task_ids=None,
     if fire == "torch":
         gen = torch.Generator(device=dev)
         gen.manual_seed(seed)
+    rng = np.random.default_rng(seed)  # host draws: pruning orders (src/nca/rollout.py:103)
 
     record = rc.record_every > 0
     steps = list(range(rc.record_every, rc.depth + 1, rc.record_every)) if record else []
     if record and (not steps or steps[-1] != rc.depth):
         steps.append(rc.depth)
     T = len(steps)
-    prune_every = int(rc.pruning["every"]) if rc.pruning else 0
-    n_cap = int(rc.pruning.get("n_cap", 2)) if rc.pruning else 0
-    prune_steps = set(range(prune_every, rc.depth, prune_every)) if prune_every else set()
+    prune_mode, prune_steps, n_cap = _prune_steps(rc)
 
     out_pred = np.zeros((N, K, H, W), dtype=np.int64)
     out_conf = np.zeros((N, K), dtype=np.float32)
     out_alive = np.ones((N, K), dtype=bool)
     out_upd = np.zeros((N, K), dtype=np.float64)
-    tr = {k: [] for k in ("exact", "cell", "conf", "upd")}
+    tr_exact = np.zeros((N, K, T), dtype=bool) if record else None
+    tr_cell = np.zeros((N, K, T), dtype=np.float32) if record else None
+    tr_conf = np.zeros((N, K, T), dtype=np.float32) if record else None
+    tr_upd = np.zeros((N, K, T), dtype=np.float64) if record else None
     boards_trace = np.zeros((rc.record_boards, T, H, W), dtype=np.int64) if rc.record_boards else None
     boundaries = sorted({rc.depth, *steps, *prune_steps})
 
@@ -166,16 +189,28 @@ def rollout(model, task: Task, boards: Boards, rc, seed: int = 0, task_ids=None,
             eng.init_state(st, batch)
         targets = torch.from_numpy(sub.targets).to(dev)
         updates = torch.zeros(B, dtype=torch.int32, device=dev)
-        p_tr = {k: [] for k in tr}
+        # Compaction (halving): row r of the live batch is (board, trial) idx[r] of this pass.
+        idx = torch.arange(B, device=dev)
+        # results of the pass by (board, trial), kept on the device until the pass ends
+        r_pred = torch.zeros((B, HW), dtype=torch.uint8, device=dev)
+        r_conf = torch.zeros(B, dtype=torch.float32, device=dev)
+        r_upd = torch.zeros(B, dtype=torch.float64, device=dev)
+        r_alive = torch.ones(B, dtype=torch.bool, device=dev)
+        if record:
+            t_exact = torch.zeros((B, T), dtype=torch.bool, device=dev)
+            t_cell = torch.zeros((B, T), dtype=torch.float32, device=dev)
+            t_conf = torch.zeros((B, T), dtype=torch.float32, device=dev)
+            t_upd = torch.zeros((B, T), dtype=torch.float64, device=dev)
         t = 0
         t_rec = 0
         for bnd in boundaries:
             n_steps = bnd - t
+            Bc = int(idx.numel())
             kw = dict(seed=seed, step0=t, updates=updates, p_fire=p_fire)
             if adaptive is not None:
                 kw["adaptive"] = (float(adaptive.get("scale", 0.9)), float(adaptive.get("bias", 0.1)))
             if fire == "torch":
-                u = torch.stack([torch.rand((B, 1, H, W), generator=gen, device=dev).reshape(B, HW)
+                u = torch.stack([torch.rand((Bc, 1, H, W), generator=gen, device=dev).reshape(Bc, HW)
                                  for _ in range(n_steps)])
                 if adaptive is None:
                     eng.run(st, batch, n_steps, mode="mask", masks=(u < p_fire).to(torch.uint8), **kw)
@@ -184,38 +219,64 @@ def rollout(model, task: Task, boards: Boards, rc, seed: int = 0, task_ids=None,
             else:
                 eng.run(st, batch, n_steps, mode="adaptive" if adaptive is not None else "philox", **kw)
             t = bnd
-            if t in prune_steps:
+            if t in prune_steps and prune_mode == "refill":
                 r = eng.readout(st, batch)
                 src, _ = eng.prune_refill(st, r["pred"], r["board_conf"], n, K, n_cap)
                 updates = updates.index_select(0, src.long())  # a clone continues its source's count
+            elif t in prune_steps:
+                # halving with compaction (src/nca/rollout.py:249-275)
+                r = eng.readout(st, batch, targets=targets)
+                per_board = np.bincount(torch.div(idx, K, rounding_mode="floor").cpu().numpy(),
+                                        minlength=n)
+                keep = eng.halving(r["pred"], r["board_conf"], per_board, n_cap, rng).bool()
+                drop = ~keep
+                if bool(drop.any()):
+                    rows = idx[drop]
+                    r_pred[rows] = r["pred"][drop]
+                    r_conf[rows] = r["board_conf"][drop]
+                    r_upd[rows] = updates[drop].double()
+                    r_alive[rows] = False
+                    if record and t_rec < T:
+                        # a trajectory that leaves keeps its last values for the remaining records
+                        t_exact[rows, t_rec:] = r["exact"][drop].bool()[:, None]
+                        t_cell[rows, t_rec:] = r["cell_acc"][drop][:, None]
+                        t_conf[rows, t_rec:] = r["board_conf"][drop][:, None]
+                        t_upd[rows, t_rec:] = updates[drop].double()[:, None]
+                    sel = keep.nonzero().squeeze(1)
+                    st = eng.gather(st, sel)
+                    batch = eng.compacted(batch, sel)
+                    updates = updates[sel]
+                    idx = idx[sel]
             if record and T and t_rec < T and t == steps[t_rec]:
                 r = eng.readout(st, batch, targets=targets)
-                p_tr["exact"].append(r["exact"].bool())
-                p_tr["cell"].append(r["cell_acc"])
-                p_tr["conf"].append(r["board_conf"])
-                p_tr["upd"].append(updates.double())
+                t_exact[idx, t_rec] = r["exact"].bool()
+                t_cell[idx, t_rec] = r["cell_acc"]
+                t_conf[idx, t_rec] = r["board_conf"]
+                t_upd[idx, t_rec] = updates.double()
                 if boards_trace is not None and start < rc.record_boards:
+                    # the first trial of the first boards (its last decoded grid if it was pruned)
+                    r_pred[idx] = r["pred"]
                     nb = min(n, rc.record_boards - start)
-                    dec = r["pred"].reshape(n, K, H, W)[:nb, 0].long().cpu().numpy()
+                    dec = r_pred.reshape(n, K, H, W)[:nb, 0].long().cpu().numpy()
                     boards_trace[start : start + nb, t_rec] = dec
                 t_rec += 1
         r = eng.readout(st, batch)
         eng.check()
-        out_pred[start : start + n] = r["pred"].reshape(n, K, H, W).long().cpu().numpy()
-        out_conf[start : start + n] = r["board_conf"].reshape(n, K).cpu().numpy()
-        out_upd[start : start + n] = updates.double().reshape(n, K).cpu().numpy()
-        for k in tr:
-            if p_tr[k]:
-                tr[k].append(torch.stack(p_tr[k], dim=1).reshape(n, K, -1).cpu().numpy())
+        r_pred[idx] = r["pred"]
+        r_conf[idx] = r["board_conf"]
+        r_upd[idx] = updates.double()
+        out_pred[start : start + n] = r_pred.reshape(n, K, H, W).long().cpu().numpy()
+        out_conf[start : start + n] = r_conf.reshape(n, K).cpu().numpy()
+        out_upd[start : start + n] = r_upd.reshape(n, K).cpu().numpy()
+        out_alive[start : start + n] = r_alive.reshape(n, K).cpu().numpy()
+        if record:
+            tr_exact[start : start + n] = t_exact.reshape(n, K, T).cpu().numpy()
+            tr_cell[start : start + n] = t_cell.reshape(n, K, T).cpu().numpy()
+            tr_conf[start : start + n] = t_conf.reshape(n, K, T).cpu().numpy()
+            tr_upd[start : start + n] = t_upd.reshape(n, K, T).cpu().numpy()
 
-    def cat(k, dtype):
-        return np.concatenate(tr[k], axis=0).astype(dtype) if record else None
-
-    return RolloutResult(
-        out_pred, out_conf, out_alive, out_upd, np.array(steps),
-        cat("exact", bool), cat("cell", np.float32), cat("conf", np.float32), cat("upd", np.float64),
-        boards_trace, None,
-    )
+    return RolloutResult(out_pred, out_conf, out_alive, out_upd, np.array(steps), tr_exact,
+                         tr_cell, tr_conf, tr_upd, boards_trace, None)
 
 
 def decode_boards(model, task: Task, x: torch.Tensor, given: torch.Tensor, inputs: torch.Tensor):

@@ -310,6 +310,60 @@ def rollout(p: dict, inputs, given, k: int, depth: int, *, channels: int, masks=
     return {"x": x, "decoded": dec, "conf": board_confidence(x, p), "updates": updates}
 
 
+def rollout_halving(p: dict, inputs, given, k: int, depth: int, *, channels: int, seed=0,
+                    p_fire=0.5, m=4, n_cap=3, inst_offset=0):
+    """Rollout with the reference's pruning (src/nca/rollout.py:154-158, 249-275): at the m - 1
+    checkpoints i * (depth // m) the alive trials of every board are halved by
+    niche_capped_pruning with rng = default_rng(seed) (rollout.py:103) and the batch is compacted.
+    Firing is the kernel's Philox stream keyed by the trial's original index, so a compacted
+    trial keeps its stream.  Returns decoded (B, H, W), conf (B,), updates (B,), alive (B,) by
+    original index; a pruned trial keeps its values from the checkpoint where it left."""
+    rng = np.random.default_rng(seed)
+    inputs_k = np.repeat(inputs, k, axis=0)
+    given_k = np.repeat(given, k, axis=0)
+    x, _, clamp = init_state(inputs_k, given_k, p, channels)
+    B, _, H, W = x.shape
+    n = B // k
+    xs = np.ascontiguousarray(x.transpose(0, 2, 3, 1))
+    clamp_s = np.ascontiguousarray(clamp.transpose(0, 2, 3, 1))
+    nchw = lambda a: np.ascontiguousarray(a.transpose(0, 3, 1, 2))  # noqa: E731
+    dt = depth // m
+    checkpoints = {i * dt for i in range(1, m)}
+    idx = np.arange(B)
+    updates = np.zeros(B, dtype=np.int64)
+    out_dec = np.zeros((B, H, W), dtype=np.int64)
+    out_conf = np.zeros(B, dtype=F32)
+    out_upd = np.zeros(B, dtype=np.int64)
+    alive = np.ones(B, dtype=bool)
+    for t in range(depth):
+        fm = philox_uniform(seed, inst_offset + idx[:, None], np.arange(H * W)[None, :], t)
+        fm = (fm < F32(p_fire)).reshape(-1, H, W)
+        updates += fm.reshape(len(idx), -1).sum(axis=1)
+        xs = step_nhwc(xs, given_k[idx], clamp_s[idx], fm, p)
+        if (t + 1) in checkpoints:
+            x = nchw(xs)
+            dec = decode_boards(x, given_k[idx], inputs_k[idx], p)
+            conf = board_confidence(x, p)
+            dec_full = np.zeros((B, H, W), dtype=np.int64)
+            conf_full = np.full(B, -np.inf, dtype=F32)
+            alive_full = np.zeros(B, dtype=bool)
+            dec_full[idx], conf_full[idx], alive_full[idx] = dec, conf, True
+            keep_full = niche_capped_pruning(dec_full.reshape(n, k, H, W), conf_full.reshape(n, k),
+                                             alive_full.reshape(n, k), n_cap, rng.permutation)
+            keep = keep_full.reshape(B)[idx]
+            drop = ~keep
+            out_dec[idx[drop]] = dec[drop]
+            out_conf[idx[drop]] = conf[drop]
+            out_upd[idx[drop]] = updates[drop]
+            alive[idx[drop]] = False
+            xs, updates, idx = xs[keep].copy(), updates[keep].copy(), idx[keep]
+    x = nchw(xs)
+    out_dec[idx] = decode_boards(x, given_k[idx], inputs_k[idx], p)
+    out_conf[idx] = board_confidence(x, p)
+    out_upd[idx] = updates
+    return {"decoded": out_dec, "conf": out_conf, "updates": out_upd, "alive": alive}
+
+
 def params_from_arrays(d: dict, cfg) -> dict:
     """Oracle parameter dict from the reference-named arrays of a model config."""
     n_out = len(cfg.output_tokens)

@@ -36,7 +36,7 @@ def test_exports_every_declared_symbol(lib):
 
 
 def test_abi_and_status_strings(lib):
-    assert lib.nca_b200_abi_version() == 1
+    assert lib.nca_b200_abi_version() == L.ABI_VERSION
     assert lib.nca_b200_status_string(4).decode().startswith("a bounded wait")
     assert lib.nca_b200_status_string(0).decode() == "ok"
 

@@ -110,3 +110,16 @@ def test_philox_uniform_range_and_rate():
     u = O.philox_uniform(123, np.arange(64)[:, None], np.arange(900)[None, :], 7)
     assert u.dtype == np.float32 and u.min() >= 0 and u.max() < 1
     assert abs(float((u < 0.5).mean()) - 0.5) < 0.01
+
+
+def test_rollout_halving_halves_alive_trials_per_checkpoint():
+    from ncas_b200.tasks import maze_boards
+
+    cfg = model_config("maze")
+    p = O.params_from_arrays(synthetic_params(cfg, 0), cfg)
+    boards = maze_boards(3, 9, seed=2)
+    out = O.rollout_halving(p, boards.inputs, boards.given, 8, 8, channels=32, seed=1, m=2, n_cap=8)
+    alive = out["alive"].reshape(3, 8)
+    # one checkpoint: floor(8 / 2) survivors per board (n_cap large enough to never bind)
+    assert np.array_equal(alive.sum(axis=1), [4, 4, 4])
+    assert out["decoded"].shape == (24, 9, 9) and np.all(out["updates"] > 0)

@@ -54,7 +54,11 @@ typedef enum NcaFireMode {
   NCA_FIRE_MASK = 0,              /* external {0,1} masks [n_steps][n_inst][H*W] uint8 */
   NCA_FIRE_PHILOX = 1,            /* u < p_fire, u from in-kernel Philox4x32-10 */
   NCA_FIRE_ADAPTIVE_PHILOX = 2,   /* u < scale * (1 - conf) + bias, u from Philox */
-  NCA_FIRE_ADAPTIVE_UNIFORM = 3   /* same rule, u from external uniforms [n_steps][n_inst][H*W] */
+  NCA_FIRE_ADAPTIVE_UNIFORM = 3,  /* same rule, u from external uniforms [n_steps][n_inst][H*W] */
+  NCA_FIRE_THRESHOLD_PHILOX = 4,  /* the reference's threshold rule (src/nca/model.py:566-593):
+                                     u < (conf > tau || given && given_confident ? p_low :
+                                     p_fire), u from Philox */
+  NCA_FIRE_THRESHOLD_UNIFORM = 5  /* same rule, u from external uniforms */
 } NcaFireMode;
 
 /* The cell rule: KernelPerception (4 heads of 3x3 taps, zero padding) + MLPUpdate + mlp head.
@@ -104,15 +108,32 @@ typedef struct NcaState {
                                nca_b200_state_bind and nca_b200_state_load_nchw) */
 } NcaState;
 
+typedef enum NcaNoiseMode {
+  NCA_NOISE_NONE = 0,
+  NCA_NOISE_PHILOX = 1,     /* in-kernel: Philox draws for instance, cell and Gaussian values */
+  NCA_NOISE_EXTERNAL = 2    /* caller's noise tensor (the reference's torch stream) */
+} NcaNoiseMode;
+
 typedef struct NcaFireDesc {
   int32_t mode;             /* NcaFireMode */
   float p_fire;             /* RolloutConfig.fire_rate */
   float adapt_scale, adapt_bias;  /* p = scale * (1 - conf_cell) + bias */
+  float p_low, tau;         /* threshold rule: RolloutConfig.p_low, RolloutConfig.tau */
+  int32_t given_confident;  /* threshold rule: given cells count as confident */
   uint64_t seed;            /* Philox key */
   int64_t step0;            /* absolute index of the first step of this call */
   const uint8_t* masks;     /* device [n_steps][n_inst][H*W] (NCA_FIRE_MASK) */
   const float* uniforms;    /* device [n_steps][n_inst][H*W] (NCA_FIRE_ADAPTIVE_UNIFORM) */
   uint32_t* updates;        /* optional device [n_inst]: fired cells are added here */
+  /* Test-time state noise (src/nca/perturb.py:23-40, added after the update and before the
+   * clamp, src/nca/model.py:544-546), on steps with absolute index < noise_until: */
+  int32_t noise_mode;       /* NcaNoiseMode */
+  float noise_p_t;          /* probability that an instance is perturbed at a step */
+  float noise_p_s;          /* probability that a cell of a perturbed instance is */
+  float noise_sigma;        /* standard deviation of the Gaussian values */
+  int64_t noise_until;
+  const float* noise;       /* NCA_NOISE_EXTERNAL: device [n_inst][C][H*W] noise of the single
+                               step of the call (n_steps must be 1) */
 } NcaFireDesc;
 
 /* ---- library / device --------------------------------------------------------------------- */
@@ -186,6 +207,13 @@ int32_t nca_b200_prune_refill(const uint8_t* pred, const float* board_conf, int3
  * x[sel] of src/nca/rollout.py:270-274, without compaction).  In place: every source must map to
  * itself (src[src[i]] == src[i]), as the maps written by nca_b200_prune_refill do. */
 int32_t nca_b200_clone(NcaState* st, const int32_t* src, void* stream);
+
+/* Damage event (src/nca/rollout.py:206-212, src/nca/perturb.py:43-83): every channel of the
+ * cells with masks[row][cell] != 0 is set to zero in every instance of that board row, then the
+ * clamp of the given cells is applied again (src/nca/model.py:430-438).  masks: device
+ * [rows][H*W] uint8 (the reference's circular_masks, one per board). */
+int32_t nca_b200_damage(const NcaModelDesc* m, const NcaBatchDesc* b, NcaState* st,
+                        const uint8_t* masks, void* stream);
 
 /* Niche-Capped Diversity Pruning, halving variant (src/nca/pruning.py:22-65), in two calls
  * around the host's random draws.  The alive trials of board n are the rows

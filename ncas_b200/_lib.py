@@ -30,6 +30,8 @@ STATUS_NAMES = {
 }
 PREC_BF16, PREC_SPLIT = 0, 1
 FIRE_MASK, FIRE_PHILOX, FIRE_ADAPTIVE_PHILOX, FIRE_ADAPTIVE_UNIFORM = 0, 1, 2, 3
+FIRE_THRESHOLD_PHILOX, FIRE_THRESHOLD_UNIFORM = 4, 5
+NOISE_NONE, NOISE_PHILOX, NOISE_EXTERNAL = 0, 1, 2
 
 
 class NcaModelDesc(C.Structure):
@@ -88,11 +90,20 @@ class NcaFireDesc(C.Structure):
         ("p_fire", C.c_float),
         ("adapt_scale", C.c_float),
         ("adapt_bias", C.c_float),
+        ("p_low", C.c_float),
+        ("tau", C.c_float),
+        ("given_confident", C.c_int32),
         ("seed", C.c_uint64),
         ("step0", C.c_int64),
         ("masks", C.c_void_p),
         ("uniforms", C.c_void_p),
         ("updates", C.c_void_p),
+        ("noise_mode", C.c_int32),
+        ("noise_p_t", C.c_float),
+        ("noise_p_s", C.c_float),
+        ("noise_sigma", C.c_float),
+        ("noise_until", C.c_int64),
+        ("noise", C.c_void_p),
     ]
 
 
@@ -144,6 +155,7 @@ SIGNATURES = {
     "nca_b200_select": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _I, _P, _P]),
     "nca_b200_prune_refill": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P]),
     "nca_b200_clone": (_I, [C.POINTER(NcaState), _P, _P]),
+    "nca_b200_damage": (_I, [C.POINTER(NcaModelDesc), C.POINTER(NcaBatchDesc), C.POINTER(NcaState), _P, _P]),
     "nca_b200_niches": (_I, [_P, _P, _P, _I, _I, _I, _P, _P, _P, _P]),
     "nca_b200_halving": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _P]),
     "nca_b200_gather": (_I, [C.POINTER(NcaState), C.POINTER(NcaState), _P, _P]),

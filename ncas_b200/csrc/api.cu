@@ -80,6 +80,28 @@ __global__ void clamp_fix_kernel(float* master, uint16_t* mirror, int C, long lo
   }
 }
 
+// Damage (src/nca/rollout.py:206-212): one thread per cell; a masked cell gets a zero state, and
+// a given cell its clamp values again.
+__global__ void damage_kernel(float* master, uint16_t* mirror, int C, long long total, int hw,
+                              NcaBatchDesc b, int c_in, int in_off, const uint8_t* masks) {
+  const long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= total) return;
+  const int inst = (int)(g / hw);
+  const int p = (int)(g - (long long)inst * hw);
+  const int row = b.inst_row ? b.inst_row[inst] : inst / b.trials;
+  if (!masks[(long long)row * hw + p]) return;
+  const long long t = g >> 7;
+  const int m = (int)(g & 127);
+  const bool gv = b.given[(long long)row * hw + p] != 0;
+  for (int c = 0; c < C; ++c) {
+    const int ci = c - in_off;
+    const float v = (gv && ci >= 0 && ci < c_in) ? b.clamp[((long long)row * hw + p) * c_in + ci] : 0.f;
+    master[((t * (C / 4) + (c >> 2)) * kTileM + m) * 4 + (c & 3)] = v;
+    if (mirror)
+      mirror[((t * (C / 8) + (c >> 3)) * kTileM + m) * 8 + (c & 7)] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  }
+}
+
 // One thread per (tile, 8-channel group, row): writes 8 channels of one cell.
 // mode 0: zero state + clamp; mode 1: load from NCHW.
 __global__ void state_fill_kernel(float* master, uint16_t* mirror, int C, long long n_tiles,
@@ -508,10 +530,19 @@ int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaState* st,
   A.p_fire = fire->p_fire;
   A.ad_scale = fire->adapt_scale;
   A.ad_bias = fire->adapt_bias;
+  A.p_low = fire->p_low;
+  A.tau = fire->tau;
+  A.given_confident = fire->given_confident;
   A.seed = fire->seed;
   A.masks = fire->masks;
   A.uniforms = fire->uniforms;
   A.updates = fire->updates;
+  A.noise_mode = fire->noise_mode;
+  A.noise_p_t = fire->noise_p_t;
+  A.noise_p_s = fire->noise_p_s;
+  A.noise_sigma = fire->noise_sigma;
+  A.noise_until = fire->noise_until;
+  A.noise = fire->noise;
   A.ctrl = ctrl;
   A.timeout_ns = (unsigned long long)(timeout_ms > 0 ? timeout_ms : 10000) * 1000000ull;
 
@@ -703,19 +734,32 @@ int32_t nca_b200_run_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaStat
   if (b->n_inst != st->n_inst || b->height * b->width != st->hw || m->channels != st->channels)
     return NCA_ERR_INVALID;
   if (fire->mode == NCA_FIRE_MASK && !fire->masks) return NCA_ERR_INVALID;
-  if (fire->mode == NCA_FIRE_ADAPTIVE_UNIFORM && !fire->uniforms) return NCA_ERR_INVALID;
-  if (fire->mode < 0 || fire->mode > 3) return NCA_ERR_INVALID;
+  if ((fire->mode == NCA_FIRE_ADAPTIVE_UNIFORM || fire->mode == NCA_FIRE_THRESHOLD_UNIFORM) &&
+      !fire->uniforms)
+    return NCA_ERR_INVALID;
+  if (fire->mode < 0 || fire->mode > 5) return NCA_ERR_INVALID;
   if (n_steps == 0) return NCA_OK;
   const bool split = st->precision == NCA_PREC_SPLIT;
   cudaStream_t s = as_stream(stream);
   const int C = m->channels, HD = m->hidden;
+  if (fire->noise_mode < 0 || fire->noise_mode > 2) return NCA_ERR_INVALID;
+  if (fire->noise_mode == NCA_NOISE_EXTERNAL && (!fire->noise || n_steps != 1)) return NCA_ERR_INVALID;
+  const bool noise = fire->noise_mode != NCA_NOISE_NONE;
   auto launch = [&](int32_t n, const NcaFireDesc* f) -> int32_t {
-    if (C == 32 && HD == 128)
+    if (C == 32 && HD == 128) {
+      if (noise)
+        return split ? launch_steps<StepCfg<32, 128, true, true>>(m, b, st, n, f, ctrl, timeout_ms, s)
+                     : launch_steps<StepCfg<32, 128, false, true>>(m, b, st, n, f, ctrl, timeout_ms, s);
       return split ? launch_steps<StepCfg<32, 128, true>>(m, b, st, n, f, ctrl, timeout_ms, s)
                    : launch_steps<StepCfg<32, 128, false>>(m, b, st, n, f, ctrl, timeout_ms, s);
-    if (C == 64 && HD == 256)
+    }
+    if (C == 64 && HD == 256) {
+      if (noise)
+        return split ? launch_steps<StepCfg<64, 256, true, true>>(m, b, st, n, f, ctrl, timeout_ms, s)
+                     : launch_steps<StepCfg<64, 256, false, true>>(m, b, st, n, f, ctrl, timeout_ms, s);
       return split ? launch_steps<StepCfg<64, 256, true>>(m, b, st, n, f, ctrl, timeout_ms, s)
                    : launch_steps<StepCfg<64, 256, false>>(m, b, st, n, f, ctrl, timeout_ms, s);
+    }
     return NCA_ERR_UNSUPPORTED;
   };
   if (st->clamped) return launch(n_steps, fire);
@@ -792,6 +836,18 @@ int32_t nca_b200_clone(NcaState* st, const int32_t* src, void* stream) {
   const int bs = 256;
   clone_kernel<<<(unsigned)((n + bs - 1) / bs), bs, 0, as_stream(stream)>>>(
       st->master[st->cur], st->mirror[st->cur], st->channels, st->hw, st->n_inst, src);
+  return cuda_status(cudaGetLastError());
+}
+
+int32_t nca_b200_damage(const NcaModelDesc* m, const NcaBatchDesc* b, NcaState* st,
+                        const uint8_t* masks, void* stream) {
+  if (!model_ok(m) || !batch_ok(b) || !st || !masks) return NCA_ERR_INVALID;
+  if (b->n_inst != st->n_inst || b->height * b->width != st->hw || m->channels != st->channels)
+    return NCA_ERR_INVALID;
+  const long long total = (long long)st->n_inst * st->hw;
+  damage_kernel<<<(unsigned)((total + 255) / 256), 256, 0, as_stream(stream)>>>(
+      st->master[st->cur], st->mirror[st->cur], st->channels, total, st->hw, *b, m->c_in,
+      m->in_offset, masks);
   return cuda_status(cudaGetLastError());
 }
 

@@ -275,4 +275,30 @@ __host__ __device__ __forceinline__ float philox_uniform(uint64_t seed, int64_t 
   return (float)(o.x >> 8) * (1.0f / 16777216.0f);
 }
 
+// Philox streams of the test-time noise, separated from the fire stream by a tag in the top
+// byte of the third counter word (instance indices stay below 2^56): tag 1 draws whether an
+// instance is perturbed at a step, tag 2 whether a cell is, tag 3 the Gaussian values.
+__host__ __device__ __forceinline__ U4 philox_tagged(uint64_t seed, uint32_t tag, int64_t inst,
+                                                     uint32_t a, int64_t step) {
+  U4 c{a, (uint32_t)inst, ((uint32_t)((uint64_t)inst >> 32) & 0xFFFFFFu) | (tag << 24),
+       (uint32_t)step};
+  return philox4x32_10(c, (uint32_t)seed, (uint32_t)(seed >> 32));
+}
+__host__ __device__ __forceinline__ float u24(uint32_t x) {
+  return (float)(x >> 8) * (1.0f / 16777216.0f);
+}
+// Four N(0, 1) values from one Philox output by the Box-Muller transform on (u, v) pairs with
+// u = ((x >> 8) + 0.5) / 2^24 in (0, 1).
+__device__ __forceinline__ float4 normal4(U4 o) {
+  const float u0 = ((float)(o.x >> 8) + 0.5f) * (1.0f / 16777216.0f);
+  const float v0 = (float)(o.y >> 8) * (1.0f / 16777216.0f);
+  const float u1 = ((float)(o.z >> 8) + 0.5f) * (1.0f / 16777216.0f);
+  const float v1 = (float)(o.w >> 8) * (1.0f / 16777216.0f);
+  const float r0 = sqrtf(-2.0f * logf(u0)), r1 = sqrtf(-2.0f * logf(u1));
+  float s0, c0, s1, c1;
+  sincospif(2.0f * v0, &s0, &c0);
+  sincospif(2.0f * v1, &s1, &c1);
+  return make_float4(r0 * c0, r0 * s0, r1 * c1, r1 * s1);
+}
+
 }  // namespace nca

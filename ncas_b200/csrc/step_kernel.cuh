@@ -36,9 +36,10 @@ constexpr int pow2ceil(int v) {
   return p;
 }
 
-template <int C_, int HD_, bool SPLIT_>
+template <int C_, int HD_, bool SPLIT_, bool NOISE_ = false>
 struct StepCfg {
   static constexpr int C = C_;
+  static constexpr bool NOISE = NOISE_;  // test-time state noise (a separate instantiation)
   static constexpr int P = 4 * C_;
   static constexpr int HD = HD_;
   static constexpr bool SPLIT = SPLIT_;
@@ -106,11 +107,16 @@ struct StepArgs {
   uint16_t* mirror[2];
   int cur;
   int fire_mode;
-  float p_fire, ad_scale, ad_bias;
+  float p_fire, ad_scale, ad_bias, p_low, tau;
+  int given_confident;
   unsigned long long seed;
   const uint8_t* masks;
   const float* uniforms;
   unsigned* updates;
+  int noise_mode;
+  float noise_p_t, noise_p_s, noise_sigma;
+  long long noise_until;
+  const float* noise;
   int* ctrl;
   unsigned long long timeout_ns;
 };
@@ -219,14 +225,16 @@ __device__ __forceinline__ void fixed_taps4(float a, float b, float c, float d, 
   lap = s * 0.0625f;
 }
 
-// Adaptive firing of one cell at step s (continuous rule on the reference's confidence,
-// src/nca/model.py:584-593, 624-629): conf = max softmax of the head scores of the cell's fp32
-// state, p = scale * (1 - conf) + bias, fire when u < p with u from Philox or from the caller.
+// Adaptive firing of one cell at step s on the reference's confidence (src/nca/model.py:624-629,
+// max softmax of the head scores of the cell's fp32 state): the continuous rule
+// p = scale * (1 - conf) + bias, or the reference's threshold rule (src/nca/model.py:566-593)
+// p = p_low for confident cells (conf > tau, or given cells when given_confident), else p_fire;
+// fire when u < p with u from Philox or from the caller.
 // Read from the fp32 state of the step's input buffer (complete since the last grid barrier).
 // The loops run to the compile-time maximum with uniform exits, so the slice stays in registers.
 template <class Cfg>
 __device__ __forceinline__ bool adaptive_fire(const StepArgs& A, int s, long long t, int m, int inst,
-                                              int p) {
+                                              int p, bool given) {
   const float* xin = A.master[(A.cur + s) & 1];
   float xs[16];
 #pragma unroll
@@ -255,9 +263,14 @@ __device__ __forceinline__ bool adaptive_fire(const StepArgs& A, int s, long lon
   for (int o = 0; o < 16; ++o)
     if (o < A.n_out) den += expf(score(o) - mx);
   const float conf = fminf(fmaxf(1.f / den, 0.f), 1.f);
-  const float prob = A.ad_scale * (1.f - conf) + A.ad_bias;
-  const float u = A.fire_mode == 3 ? A.uniforms[((long long)s * A.n_inst + inst) * A.HW + p]
-                                   : philox_uniform(A.seed, A.inst_offset + (A.inst_id ? A.inst_id[inst] : inst), p, A.step0 + s);
+  float prob;
+  if (A.fire_mode >= 4)  // threshold rule: confident cells fire at p_low
+    prob = (conf > A.tau || (given && A.given_confident)) ? A.p_low : A.p_fire;
+  else
+    prob = A.ad_scale * (1.f - conf) + A.ad_bias;
+  const bool ext = A.fire_mode == 3 || A.fire_mode == 5;
+  const float u = ext ? A.uniforms[((long long)s * A.n_inst + inst) * A.HW + p]
+                      : philox_uniform(A.seed, A.inst_offset + (A.inst_id ? A.inst_id[inst] : inst), p, A.step0 + s);
   return u < prob;
 }
 
@@ -666,8 +679,9 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           uint32_t fl = 0;
           if (valid) {
             const int row = A.inst_row ? A.inst_row[inst] : (int)fdiv((unsigned)inst, A.div_k);
-            fl = 4u | (A.given[(long long)row * A.HW + p] ? 2u : 0u);
-            fl |= adaptive_fire<Cfg>(A, s, t, m, inst, p) ? 1u : 0u;
+            const bool gv = A.given[(long long)row * A.HW + p] != 0;
+            fl = 4u | (gv ? 2u : 0u);
+            fl |= adaptive_fire<Cfg>(A, s, t, m, inst, p, gv) ? 1u : 0u;
           }
           s_flags[(it & 3) * kTileM + m] = (uint8_t)fl;
           __syncwarp();
@@ -781,6 +795,23 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           // registers than packing all of them first)
           uint4* mout4 = reinterpret_cast<uint4*>(mout) + ((t * (Cfg::C / 8) + half * (CH / 8)) << 7) + m;
           uint32_t pk[4];
+          // Test-time noise (src/nca/perturb.py:23-40): added after the update, before the clamp
+          // (src/nca/model.py:544-546); only the NOISE instantiation carries this code.
+          bool nz = false;
+          int p_cell = 0;
+          long long nid = 0;
+          if constexpr (Cfg::NOISE) {
+            p_cell = (int)(g - (unsigned)inst * A.HW);
+            nid = A.inst_offset + (A.inst_id ? A.inst_id[inst] : inst);
+            const long long step = A.step0 + s;
+            if (A.noise_mode == 1) {
+              nz = step < A.noise_until &&
+                   u24(philox_tagged(A.seed, 1u, nid, 0u, step).x) < A.noise_p_t &&
+                   u24(philox_tagged(A.seed, 2u, nid, (uint32_t)p_cell, step).x) < A.noise_p_s;
+            } else if (A.noise_mode == 2) {
+              nz = true;
+            }
+          }
 #pragma unroll
           for (int q = 0; q < NQ; ++q) {
             const float4 b = bb[q];
@@ -788,6 +819,25 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
             const float2 d1 = __fadd2_rn(f2(__uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])), f2(b.z, b.w));
             float2 y0 = __ffma2_rn(ff, d0, f2(xo[q].x, xo[q].y));
             float2 y1 = __ffma2_rn(ff, d1, f2(xo[q].z, xo[q].w));
+            if constexpr (Cfg::NOISE) {
+              if (nz) {
+                float4 e;
+                const int c0 = half * CH + 4 * q;  // first channel of this chunk
+                if (A.noise_mode == 1) {
+                  const float4 z = normal4(philox_tagged(A.seed, 3u, nid, (uint32_t)(p_cell * (Cfg::C / 4) + (c0 >> 2)),
+                                                         A.step0 + s));
+                  e = make_float4(A.noise_sigma * z.x, A.noise_sigma * z.y, A.noise_sigma * z.z,
+                                  A.noise_sigma * z.w);
+                } else {
+                  const float* nb = A.noise + ((long long)inst * Cfg::C + c0) * A.HW + p_cell;
+                  e = make_float4(nb[0], nb[A.HW], nb[2 * A.HW], nb[3 * A.HW]);
+                }
+                y0.x += e.x;
+                y0.y += e.y;
+                y1.x += e.z;
+                y1.y += e.w;
+              }
+            }
             y0.x = (keep >> (4 * q + 0)) & 1u ? xo[q].x : y0.x;
             y0.y = (keep >> (4 * q + 1)) & 1u ? xo[q].y : y0.y;
             y1.x = (keep >> (4 * q + 2)) & 1u ? xo[q].z : y1.x;

@@ -229,12 +229,21 @@ class B200Engine:
         uniforms: torch.Tensor | None = None,
         adaptive: tuple[float, float] = (0.9, 0.1),
         updates: torch.Tensor | None = None,
+        noise: dict | None = None,
+        threshold: tuple[float, float, bool] | None = None,
     ) -> None:
         """n_steps NCA steps.  mode: 'mask' (masks (n_steps, n_inst, H*W) uint8), 'philox',
-        'adaptive' (Philox, p = a * (1 - conf) + b) or 'adaptive_uniform' (uniforms given)."""
+        'adaptive' (Philox, p = a * (1 - conf) + b) or 'adaptive_uniform' (uniforms given);
+        'threshold' / 'threshold_uniform': the reference's rule with threshold = (p_low, tau,
+        given_confident) (p_low for cells with conf > tau, p_fire for the others).
+        noise (test-time state noise): {'p_t', 'p_s', 'sigma', 'until'} drawn in the kernel
+        from Philox, or {'tensor': (n_inst, C, H*W) fp32} for a single step."""
         f = L.NcaFireDesc()
         f.mode = {"mask": L.FIRE_MASK, "philox": L.FIRE_PHILOX, "adaptive": L.FIRE_ADAPTIVE_PHILOX,
-                  "adaptive_uniform": L.FIRE_ADAPTIVE_UNIFORM}[mode]
+                  "adaptive_uniform": L.FIRE_ADAPTIVE_UNIFORM, "threshold": L.FIRE_THRESHOLD_PHILOX,
+                  "threshold_uniform": L.FIRE_THRESHOLD_UNIFORM}[mode]
+        if threshold is not None:
+            f.p_low, f.tau, f.given_confident = float(threshold[0]), float(threshold[1]), int(bool(threshold[2]))
         f.p_fire = float(p_fire)
         f.adapt_scale, f.adapt_bias = float(adaptive[0]), float(adaptive[1])
         f.seed = int(seed) & ((1 << 64) - 1)
@@ -253,6 +262,17 @@ class B200Engine:
         if updates is not None:
             assert updates.dtype == torch.int32 and updates.numel() >= b.n_inst
             f.updates = updates.data_ptr()
+        if noise is not None:
+            if "tensor" in noise:
+                nz = noise["tensor"].to(self.device, torch.float32).contiguous()
+                assert n_steps == 1 and nz.numel() == b.n_inst * self.channels * b.hw
+                keep.append(nz)
+                f.noise_mode, f.noise = L.NOISE_EXTERNAL, nz.data_ptr()
+            else:
+                f.noise_mode = L.NOISE_PHILOX
+                f.noise_p_t, f.noise_p_s = float(noise["p_t"]), float(noise["p_s"])
+                f.noise_sigma = float(noise["sigma"])
+                f.noise_until = int(noise["until"])
         L.check(
             L.lib().nca_b200_run_steps(
                 C.byref(self.desc), C.byref(b.desc), C.byref(st.st), int(n_steps), C.byref(f),
@@ -328,6 +348,15 @@ class B200Engine:
         L.check(L.lib().nca_b200_clone(C.byref(st.st), src.data_ptr(), self._s()), "nca_b200_clone")
         self.launches += 2
         return src, kept
+
+    def damage(self, st: State, b: Batch, masks: torch.Tensor) -> None:
+        """Damage event: zero state in the cells of masks (rows, H*W) (one mask per board row),
+        clamp re-applied (src/nca/rollout.py:206-212)."""
+        mk = masks.to(self.device, torch.uint8).contiguous()
+        L.check(L.lib().nca_b200_damage(C.byref(self.desc), C.byref(b.desc), C.byref(st.st),
+                                        mk.data_ptr(), self._s()), "nca_b200_damage")
+        self._keep_damage = mk
+        self.launches += 1
 
     def halving(self, pred: torch.Tensor, board_conf: torch.Tensor, rows_per_board: np.ndarray,
                 n_cap: int, rng: np.random.Generator) -> torch.Tensor:

@@ -14,7 +14,17 @@ Randomness (RolloutConfig.engine["fire"]):
                         `rand((B,1,H,W))` per step (src/nca/model.py:586), consumed in the same
                         order; the kernel applies the drawn masks.
 
-Rules beyond the reference's uniform firing:
+The reference's options on this path:
+  threshold adaptive firing: RolloutConfig.p_low / tau / given_confident (src/nca/model.py:
+      566-593), evaluated in the kernel on each cell's confidence;
+  test-time noise: RolloutConfig.noise = {"p_t", "p_s", "sigma", "r"} (src/nca/perturb.py:23-40,
+      the first r * depth steps): with fire "philox" the instance / cell / Gaussian draws come
+      from tagged Philox streams in the kernel; with fire "torch" the reference's own draws
+      (fire mask, then noise, per step) are made on the generator and applied by the kernel;
+  damage: RolloutConfig.damage_at / damage (src/nca/rollout.py:206-212): the discs are drawn
+      on the host from numpy.random.default_rng(seed), the state update is a kernel.
+
+Rules beyond the reference's:
   adaptive firing (continuous):  RolloutConfig.engine["adaptive"] = {"scale": a, "bias": b}
       p_cell = a * (1 - conf_cell) + b with conf_cell = NCA.confidence of the current state;
   niche-capped pruning with refill: RolloutConfig.pruning = {"every": s, "n_cap": c}
@@ -32,6 +42,7 @@ is renumbered.
 
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -39,6 +50,7 @@ import torch
 
 from . import _lib as L
 from .engine import B200Engine
+from .perturb import circular_masks, sample_noise
 from .tasks import Boards, Task
 
 
@@ -99,13 +111,13 @@ def _engine_for(model, opts: dict) -> B200Engine:
 
 
 def _check_config(rc) -> None:
-    if getattr(rc, "p_low", None) is not None or getattr(rc, "tau", None) is not None:
-        raise ValueError("threshold adaptive firing (p_low/tau) is not implemented by the b200 "
-                         "backend; use engine['adaptive'] for the continuous rule")
-    if getattr(rc, "noise", None) is not None:
-        raise ValueError("test-time noise is not implemented by the b200 backend")
-    if getattr(rc, "damage_at", None) is not None:
-        raise ValueError("damage events are not implemented by the b200 backend")
+    if (getattr(rc, "p_low", None) is None) != (getattr(rc, "tau", None) is None):
+        raise ValueError("threshold adaptive firing needs both p_low and tau")
+    if getattr(rc, "p_low", None) is not None and (getattr(rc, "engine", None) or {}).get("adaptive"):
+        raise ValueError("choose one adaptive rule: p_low/tau or engine['adaptive']")
+    nz = getattr(rc, "noise", None)
+    if nz is not None and not all(k in nz for k in ("p_t", "p_s", "sigma")):
+        raise ValueError("noise needs p_t, p_s and sigma (src/nca/perturb.py:23-40)")
     pr = getattr(rc, "pruning", None)
     if pr is not None and "every" not in pr and "m" not in pr:
         raise ValueError("pruning needs 'm' (halving at m - 1 checkpoints, src/nca/pruning.py) or "
@@ -139,7 +151,11 @@ def rollout(model, task: Task, boards: Boards, rc, seed: int = 0, task_ids=None,
     if fire not in ("philox", "torch"):
         raise ValueError("engine['fire'] must be 'philox' or 'torch'")
     adaptive = opts.get("adaptive")
+    thr = (float(rc.p_low), float(rc.tau), bool(rc.given_confident)) if rc.p_low is not None else None
     p_fire = cfg.fire_rate if rc.fire_rate is None else rc.fire_rate
+    noise = rc.noise
+    noise_until = int(math.ceil(float(noise.get("r", 1.0)) * rc.depth)) if noise is not None else 0
+    damage_at = rc.damage_at
     N = len(boards)
     H, W = boards.shape
     HW = H * W
@@ -167,7 +183,9 @@ def rollout(model, task: Task, boards: Boards, rc, seed: int = 0, task_ids=None,
     tr_conf = np.zeros((N, K, T), dtype=np.float32) if record else None
     tr_upd = np.zeros((N, K, T), dtype=np.float64) if record else None
     boards_trace = np.zeros((rc.record_boards, T, H, W), dtype=np.int64) if rc.record_boards else None
-    boundaries = sorted({rc.depth, *steps, *prune_steps})
+    damage_masks = np.zeros((N, H, W), dtype=bool) if damage_at is not None else None
+    boundaries = sorted({rc.depth, *steps, *prune_steps}
+                        | ({damage_at} if damage_at is not None and 0 < damage_at < rc.depth else set()))
 
     for start in range(0, N, per_pass):
         sub = boards.subset(np.arange(start, min(N, start + per_pass)))
@@ -203,21 +221,48 @@ def rollout(model, task: Task, boards: Boards, rc, seed: int = 0, task_ids=None,
             t_upd = torch.zeros((B, T), dtype=torch.float64, device=dev)
         t = 0
         t_rec = 0
+        def damage(t_now: int) -> None:
+            dmg = rc.damage
+            masks = circular_masks(n, H, W, int(dmg["n"]), float(dmg["r_min"]), float(dmg["r_max"]),
+                                   rng, geometry=dmg.get("geometry", "ours"))
+            damage_masks[start : start + n] = masks
+            eng.damage(st, batch, torch.from_numpy(masks.reshape(n, HW)).to(dev))
+
+        if damage_at == 0:
+            damage(0)
+        rule = "adaptive" if adaptive is not None else ("threshold" if thr is not None else None)
         for bnd in boundaries:
             n_steps = bnd - t
             Bc = int(idx.numel())
-            kw = dict(seed=seed, step0=t, updates=updates, p_fire=p_fire)
+            kw = dict(seed=seed, updates=updates, p_fire=p_fire)
             if adaptive is not None:
                 kw["adaptive"] = (float(adaptive.get("scale", 0.9)), float(adaptive.get("bias", 0.1)))
+            if thr is not None:
+                kw["threshold"] = thr
             if fire == "torch":
-                u = torch.stack([torch.rand((Bc, 1, H, W), generator=gen, device=dev).reshape(Bc, HW)
-                                 for _ in range(n_steps)])
-                if adaptive is None:
-                    eng.run(st, batch, n_steps, mode="mask", masks=(u < p_fire).to(torch.uint8), **kw)
-                else:
-                    eng.run(st, batch, n_steps, mode="adaptive_uniform", uniforms=u, **kw)
+                # the reference's stream: per step a fire draw, then (inside the noise window)
+                # the noise draws; the kernel applies them
+                per_step = noise is not None and t < noise_until
+                chunks = [(t + i, 1) for i in range(n_steps)] if per_step else [(t, n_steps)]
+                for t0, ns in chunks:
+                    u = torch.stack([torch.rand((Bc, 1, H, W), generator=gen, device=dev).reshape(Bc, HW)
+                                     for _ in range(ns)])
+                    nz = None
+                    if per_step and t0 < noise_until:
+                        tn = sample_noise(Bc, cfg.channels, H, W, noise["p_t"], noise["p_s"],
+                                          noise["sigma"], gen, dev)
+                        nz = None if tn is None else {"tensor": tn.reshape(Bc, cfg.channels, HW)}
+                    if rule is None:
+                        eng.run(st, batch, ns, mode="mask", masks=(u < p_fire).to(torch.uint8),
+                                step0=t0, noise=nz, **kw)
+                    else:
+                        eng.run(st, batch, ns, mode=rule + "_uniform", uniforms=u, step0=t0, noise=nz, **kw)
             else:
-                eng.run(st, batch, n_steps, mode="adaptive" if adaptive is not None else "philox", **kw)
+                nz = None
+                if noise is not None and t < noise_until:
+                    nz = {"p_t": noise["p_t"], "p_s": noise["p_s"], "sigma": noise["sigma"],
+                          "until": noise_until}
+                eng.run(st, batch, n_steps, mode=rule or "philox", step0=t, noise=nz, **kw)
             t = bnd
             if t in prune_steps and prune_mode == "refill":
                 r = eng.readout(st, batch)
@@ -260,6 +305,8 @@ def rollout(model, task: Task, boards: Boards, rc, seed: int = 0, task_ids=None,
                     dec = r_pred.reshape(n, K, H, W)[:nb, 0].long().cpu().numpy()
                     boards_trace[start : start + nb, t_rec] = dec
                 t_rec += 1
+            if damage_at is not None and t == damage_at and 0 < t < rc.depth:
+                damage(t)
         r = eng.readout(st, batch)
         eng.check()
         r_pred[idx] = r["pred"]
@@ -276,7 +323,7 @@ def rollout(model, task: Task, boards: Boards, rc, seed: int = 0, task_ids=None,
             tr_upd[start : start + n] = t_upd.reshape(n, K, T).cpu().numpy()
 
     return RolloutResult(out_pred, out_conf, out_alive, out_upd, np.array(steps), tr_exact,
-                         tr_cell, tr_conf, tr_upd, boards_trace, None)
+                         tr_cell, tr_conf, tr_upd, boards_trace, damage_masks)
 
 
 def decode_boards(model, task: Task, x: torch.Tensor, given: torch.Tensor, inputs: torch.Tensor):

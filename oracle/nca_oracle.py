@@ -73,15 +73,18 @@ def apply_clamp(x, given4, clamp, in_off: int) -> np.ndarray:
     return out
 
 
-def step_nhwc(x, given, clamp_nhwc, fire, p: dict) -> np.ndarray:
-    """NCA.step without norm/noise/clock (src/nca/model.py:503-525, residual_update 527-559)
-    on channels-last arrays: x (B, H, W, C), given (B, H, W) bool, clamp (B, H, W, c_in),
-    fire (B, H, W) {0, 1}.  x' = x + fire * dx, then the clamp."""
+def step_nhwc(x, given, clamp_nhwc, fire, p: dict, noise=None) -> np.ndarray:
+    """NCA.step without norm/clock (src/nca/model.py:503-525, residual_update 527-559) on
+    channels-last arrays: x (B, H, W, C), given (B, H, W) bool, clamp (B, H, W, c_in),
+    fire (B, H, W) {0, 1}, noise (B, H, W, C) or None.  x' = x + fire * dx (+ noise), then the
+    clamp."""
     B, H, W, C = x.shape
     z = perceive_nhwc(x, p["taps"])
     dx = mlp_rows(z.reshape(B * H * W, -1), p["w1"], p["b1"], p["w2"], p["b2"]).reshape(B, H, W, C)
     np.multiply(dx, fire.reshape(B, H, W, 1).astype(F32), out=dx)
     np.add(dx, x, out=dx)
+    if noise is not None:
+        np.add(dx, noise, out=dx)
     sl = slice(p["in_off"], p["in_off"] + clamp_nhwc.shape[-1])
     dx[..., sl] = np.where(given[..., None], clamp_nhwc, dx[..., sl])
     return dx
@@ -252,6 +255,44 @@ def philox_uniform(seed: int, inst: np.ndarray, cell: np.ndarray, step: int) -> 
     return ((o[0] >> np.uint64(8)).astype(np.float64) * (1.0 / 16777216.0)).astype(F32)
 
 
+def philox_tagged(seed: int, tag: int, inst: np.ndarray, a: np.ndarray, step: int):
+    """The kernel's noise streams: counter (a, inst_lo, inst_hi | tag << 24, step), key seed.
+    Returns the four output words."""
+    inst = np.asarray(inst, dtype=np.int64)
+    a = np.asarray(a, dtype=np.int64)
+    inst, a = np.broadcast_arrays(inst, a)
+    hi = ((inst.astype(np.uint64) >> np.uint64(32)) & np.uint64(0xFFFFFF)) | np.uint64(tag << 24)
+    ctr = (a.astype(np.uint64) & np.uint64(MASK32), inst.astype(np.uint64) & np.uint64(MASK32), hi,
+           np.full(inst.shape, step & MASK32, np.uint64))
+    return philox4x32_10(ctr, (seed & MASK32, (seed >> 32) & MASK32))
+
+
+def philox_noise(seed: int, inst_ids: np.ndarray, hw: int, channels: int, step: int, p_t: float,
+                 p_s: float, sigma: float) -> np.ndarray:
+    """Test-time noise of one step (src/nca/perturb.py:23-40) from the kernel's Philox streams:
+    instance hit when u(tag 1) < p_t, cell hit when u(tag 2) < p_s, Gaussian values by Box-Muller
+    on the words of tag 3 (counter a = cell * C/4 + channel/4, four channels per draw).
+    Returns (B, hw, C) float32."""
+    ids = np.asarray(inst_ids, dtype=np.int64)
+    B = len(ids)
+    u = lambda w: (w >> np.uint64(8)).astype(np.float64) / 16777216.0  # noqa: E731
+    act = u(philox_tagged(seed, 1, ids, np.zeros(B, np.int64), step)[0]) < np.float32(p_t)
+    cell = u(philox_tagged(seed, 2, ids[:, None], np.arange(hw)[None, :], step)[0]) < np.float32(p_s)
+    hit = act[:, None] & cell
+    C4 = channels // 4
+    a = np.arange(hw)[None, :, None] * C4 + np.arange(C4)[None, None, :]
+    o = philox_tagged(seed, 3, ids[:, None, None], a, step)
+    u0 = ((o[0] >> np.uint64(8)).astype(np.float64) + 0.5) / 16777216.0
+    v0 = (o[1] >> np.uint64(8)).astype(np.float64) / 16777216.0
+    u1 = ((o[2] >> np.uint64(8)).astype(np.float64) + 0.5) / 16777216.0
+    v1 = (o[3] >> np.uint64(8)).astype(np.float64) / 16777216.0
+    r0, r1 = np.sqrt(-2.0 * np.log(u0)), np.sqrt(-2.0 * np.log(u1))
+    z = np.stack([r0 * np.cos(2 * np.pi * v0), r0 * np.sin(2 * np.pi * v0),
+                  r1 * np.cos(2 * np.pi * v1), r1 * np.sin(2 * np.pi * v1)], axis=-1)
+    z = (z.reshape(B, hw, channels) * sigma).astype(F32)
+    return np.where(hit[:, :, None], z, F32(0))
+
+
 def philox_masks(seed: int, inst_offset: int, n_inst: int, hw: int, step: int, p: float):
     inst = inst_offset + np.arange(n_inst)[:, None]
     cell = np.arange(hw)[None, :]
@@ -268,12 +309,16 @@ def adaptive_prob(conf, scale=0.9, bias=0.1):
 # ---------------------------------------------------------------------------------- rollout
 def rollout(p: dict, inputs, given, k: int, depth: int, *, channels: int, masks=None, seed=0,
             p_fire=0.5, fire="external", inst_offset=0, uniforms=None, adaptive=None,
-            prune_every=0, n_cap=2, targets=None):
+            prune_every=0, n_cap=2, targets=None, threshold=None, noise=None, damage=None):
     """Rollout of the benchmark configs (src/nca/rollout.py:86-305 restricted to one pass, no
     noise/damage): boards repeated k times, `depth` steps, then decoded boards and board
     confidences.  fire: 'external' (masks (depth, B, H, W) {0,1}), 'philox' (kernel stream),
     'adaptive_uniform' (uniforms (depth, B, H, W)), 'adaptive_philox'.  prune_every > 0 applies
-    niche_cap_refill every prune_every steps."""
+    niche_cap_refill every prune_every steps.  threshold = (p_low, tau, given_confident) selects
+    the reference's threshold rule (src/nca/model.py:566-593) for the adaptive fire modes;
+    noise = dict(p_t, p_s, sigma, until) adds philox_noise on steps < until; damage = (t, masks
+    (n_boards, H, W) bool) zeroes the masked cells before step t and re-clamps
+    (src/nca/rollout.py:206-212)."""
     inputs_k = np.repeat(inputs, k, axis=0)
     given_k = np.repeat(given, k, axis=0)
     x, g4, clamp = init_state(inputs_k, given_k, p, channels)
@@ -283,6 +328,11 @@ def rollout(p: dict, inputs, given, k: int, depth: int, *, channels: int, masks=
     nchw = lambda a: np.ascontiguousarray(a.transpose(0, 3, 1, 2))  # noqa: E731
     updates = np.zeros(B, dtype=np.int64)
     for t in range(depth):
+        if damage is not None and t == damage[0]:
+            dm = np.repeat(np.asarray(damage[1], bool), k, axis=0)
+            xs[dm] = 0.0
+            sl = slice(p["in_off"], p["in_off"] + clamp_s.shape[-1])
+            xs[..., sl] = np.where(given_k[..., None], clamp_s, xs[..., sl])
         if fire == "external":
             fm = masks[t].reshape(B, H, W) != 0
         elif fire == "philox":
@@ -293,10 +343,22 @@ def rollout(p: dict, inputs, given, k: int, depth: int, *, channels: int, masks=
             else:
                 u = philox_uniform(seed, inst_offset + np.arange(B)[:, None], np.arange(H * W)[None, :],
                                    t).reshape(B, H, W)
-            a = adaptive or (0.9, 0.1)
-            fm = u < adaptive_prob(confidence(nchw(xs), p), *a)
+            conf = confidence(nchw(xs), p)
+            if threshold is not None:
+                p_low, tau, given_conf = threshold
+                confident = conf > F32(tau)
+                if given_conf:
+                    confident = confident | given_k
+                fm = u < np.where(confident, F32(p_low), F32(p_fire))
+            else:
+                a = adaptive or (0.9, 0.1)
+                fm = u < adaptive_prob(conf, *a)
         updates += fm.reshape(B, -1).sum(axis=1)
-        xs = step_nhwc(xs, given_k, clamp_s, fm, p)
+        nz = None
+        if noise is not None and t < noise["until"]:
+            nz = philox_noise(seed, inst_offset + np.arange(B), H * W, xs.shape[-1], t, noise["p_t"],
+                              noise["p_s"], noise["sigma"]).reshape(B, H, W, -1)
+        xs = step_nhwc(xs, given_k, clamp_s, fm, p, nz)
         if prune_every and (t + 1) % prune_every == 0 and (t + 1) < depth:
             x = nchw(xs)
             dec = decode_boards(x, given_k, inputs_k, p).reshape(-1, k, H * W)

@@ -148,6 +148,22 @@ def main() -> None:
                                2, np.random.default_rng(42))
     G.update(prune_dec=dec, prune_conf=pconf, prune_alive=palive, prune_new=new.numpy())
 
+    # ---- perturbations (damage discs, noise draws) and the threshold firing rule
+    from nca.perturb import circular_masks as ref_circular_masks  # noqa: E402
+    from nca.perturb import sample_noise as ref_sample_noise  # noqa: E402
+
+    G["dmg_ours"] = ref_circular_masks(4, 15, 13, 2, 0.1, 0.4, np.random.default_rng(21))
+    G["dmg_official"] = ref_circular_masks(3, 9, 9, 1, 0.2, 0.5, np.random.default_rng(22),
+                                           geometry="official")
+    nz = ref_sample_noise(torch.zeros((6, 8, 5, 5)), 0.6, 0.5, 0.05, torch.Generator().manual_seed(7))
+    G["noise_draw"] = nz.numpy()
+    g4_np = gv.numpy()[:, None]
+    fm_g = m.sample_fire_mask(x, 0.5, 0.1, 0.12, torch.Generator().manual_seed(3), g4)
+    fm_n = m.sample_fire_mask(x, 0.5, 0.1, 0.12, torch.Generator().manual_seed(3), None)
+    u_thr = torch.rand((8, 1, 9, 9), generator=torch.Generator().manual_seed(3))
+    G.update(thr_x=x.numpy(), thr_given=g4_np, thr_u=u_thr.numpy(), thr_mask_given=fm_g.numpy(),
+             thr_mask=fm_n.numpy())
+
     np.savez_compressed(OUT, **G)
     print(f"wrote {OUT} ({OUT.stat().st_size / 1e3:.0f} kB, {len(G)} arrays)")
 

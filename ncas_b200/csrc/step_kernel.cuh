@@ -92,6 +92,7 @@ struct StepArgs {
   int n_steps;
   long long step0;
   int stages, win_cells;
+  float pad[64];  // state of the cells outside a board (zero padding: 0), by channel
   int c_in, in_off, c_out, out_off, n_out, fixed_taps;
   float taps[4][9];
   float head_w[16][16];
@@ -129,7 +130,7 @@ struct SmemLayout {
     w1 = 0;
     w2 = w1 + Cfg::W1_BYTES;
     win = (w2 + Cfg::W2_BYTES + 1023) & ~1023;
-    b1 = (win + stages * win_cells * Cfg::ROWB + 15) & ~15;
+    b1 = (win + stages * (win_cells + 1) * Cfg::ROWB + 15) & ~15;  // + the padding cell
     b2 = b1 + Cfg::HD * 4;
     flags = b2 + Cfg::C * 4;
     bars = (flags + 4 * kTileM + 7) & ~7;
@@ -315,6 +316,22 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
     for (int r = 0; r < 4; ++r) mbar_init(&bars[BAR_FLAGS + r], 4);
     fence_mbar_init();
   }
+  // Every chunk row of a window stage ends with a padding cell (index win_cells): the stencil
+  // reads it for neighbours outside the board, so no load is predicated.
+  for (int i = threadIdx.x; i < A.stages * Cfg::NCH; i += kThreads) {
+    const int stg = i / Cfg::NCH, ch = i % Cfg::NCH;
+    uint8_t* cell = smem + L.win + (stg * (A.win_cells + 1) * Cfg::NCH + ch * (A.win_cells + 1) + A.win_cells) * 16;
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if constexpr (Cfg::SRC_BF16) {
+        w[e] = pack_bf16(A.pad[ch * 8 + 2 * e], A.pad[ch * 8 + 2 * e + 1]);
+      } else {
+        w[e] = __float_as_uint(A.pad[ch * 4 + e]);
+      }
+    }
+    *reinterpret_cast<uint4*>(cell) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
   for (int i = threadIdx.x; i < Cfg::HD; i += kThreads) s_b1[i] = A.b1[i];
   for (int i = threadIdx.x; i < Cfg::C; i += kThreads) s_b2[i] = A.b2[i];
   if (warp == 0) {
@@ -468,7 +485,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         const long long hi = (wb + WC) < total ? (wb + WC) : total;
         if (lane == 0) mbar_arrive_expect_tx(&bars[BAR_WIN_FULL + stage], (uint32_t)(NCH * (hi - lo) * 16));
         __syncwarp();
-        const uint32_t dst = smem_u32(smem + L.win + stage * WC * Cfg::ROWB);
+        const uint32_t dst = smem_u32(smem + L.win + stage * (WC + 1) * Cfg::ROWB);
         // one bulk copy per (chunk, tile overlapped by the window): 3 tiles while the board is
         // narrower than a tile, up to 2 + ceil((2W + 2) / 128) for wider boards
         const long long t0 = lo >> 7;
@@ -480,7 +497,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           const long long c_hi = ((T + 1) << 7) < hi ? ((T + 1) << 7) : hi;
           if (c_hi > c_lo) {
             const uint8_t* p = src + (((T * NCH + ch) << 7) + (c_lo & 127)) * 16;
-            bulk_g2s(dst + (uint32_t)((ch * WC + (c_lo - wb)) * 16), p, (uint32_t)((c_hi - c_lo) * 16),
+            bulk_g2s(dst + (uint32_t)((ch * (WC + 1) + (c_lo - wb)) * 16), p, (uint32_t)((c_hi - c_lo) * 16),
                      &bars[BAR_WIN_FULL + stage]);
           }
         }
@@ -518,7 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         if (!warp_wait(&bars[BAR_WIN_FULL + stage], v & 1, fs, W_ST_WINFULL)) { ok = false; break; }
         if (!warp_wait(&bars[BAR_Z_EMPTY + slot], (u & 1) ^ 1, fs, W_ST_ZEMPTY)) { ok = false; break; }
         tc_fence_after();
-        const uint8_t* win = smem + L.win + stage * WC * Cfg::ROWB;
+        const uint8_t* win = smem + L.win + stage * (WC + 1) * Cfg::ROWB;
         const unsigned g = (unsigned)t * kTileM + m;
         const bool valid = (long long)g < total;
         int i = 0, j = 0, inst = 0, p = 0;
@@ -558,22 +575,18 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           const int dy = n / 3 - 1, dx = n % 3 - 1;
           const int wc = c0 + dy * W + dx;
           nb_ok[n] = (dy < 0 ? up : (dy > 0 ? dn : valid)) && (dx < 0 ? lf : (dx > 0 ? rt : true));
-          nb_row[n] = wbase + (uint32_t)(nb_ok[n] ? wc : 0) * 16u;
+          nb_row[n] = wbase + (uint32_t)(nb_ok[n] ? wc : WC) * 16u;  // WC: the padding cell
         }
 #pragma unroll 1
         for (int q = 0; q < Cfg::NCH / 2; ++q) {
           const int ch = half * (Cfg::NCH / 2) + q;
-          const uint32_t choff = (uint32_t)(ch * WC) * 16u;
+          const uint32_t choff = (uint32_t)(ch * (WC + 1)) * 16u;
           uint4 v[9];
 #pragma unroll
-          for (int n = 0; n < 9; ++n) {
-            v[n] = make_uint4(0u, 0u, 0u, 0u);
-            if (nb_ok[n]) {
-              asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                           : "=r"(v[n].x), "=r"(v[n].y), "=r"(v[n].z), "=r"(v[n].w)
-                           : "r"(nb_row[n] + choff));
-            }
-          }
+          for (int n = 0; n < 9; ++n)
+            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(v[n].x), "=r"(v[n].y), "=r"(v[n].z), "=r"(v[n].w)
+                         : "r"(nb_row[n] + choff));
           if constexpr (Cfg::SRC_BF16) {
             // 8 channels ch*8 .. ch*8+7 as 4 bf16 pairs; identity, Sobel-x, Sobel-y, Laplacian
             uint32_t zi[4], zx[4], zy[4], zl[4];

@@ -64,7 +64,7 @@ typedef enum NcaFireMode {
 /* The cell rule: KernelPerception (4 heads of 3x3 taps, zero padding) + MLPUpdate + mlp head.
  * Mirrors nca.model.NCAConfig / NCA (src/nca/model.py:48-137, 161-178, 277-287, 344-345). */
 typedef struct NcaModelDesc {
-  int32_t channels;     /* C: 32 or 64 */
+  int32_t channels;     /* C: 16, 32 or 64 */
   int32_t perception;   /* P = 4 * C (heads = 4) */
   int32_t hidden;       /* Hd: multiple of 32, <= 256 */
   int32_t c_in, in_offset;    /* clamped input slice [in_offset, in_offset + c_in) */
@@ -78,7 +78,19 @@ typedef struct NcaModelDesc {
   const void* weights;  /* device: image written by nca_b200_pack_weights + uploaded */
   const float* b1;      /* device [hidden]   update.fc1.bias */
   const float* b2;      /* device [channels] update.fc2.bias */
+  int32_t head_kind;    /* NCA_HEAD_LINEAR: scores head_w x + head_b, softmax confidence
+                           (head "mlp"); NCA_HEAD_L2: head_w rows are the output-token embeddings
+                           (out_embed), score 1 / (1 + |x - e|), confidence the best score
+                           (src/nca/model.py:596-633) */
+  float pad[64];        /* state of the cells outside the board by channel: the wall token's
+                           embedding for wall padding (pad_vec, src/nca/model.py:140-152, 320-325),
+                           zeros for zero padding */
+  const void* weights_lo;  /* optional device image (same layout as `weights`) of the residual
+                              w - bf16(w): NCA_PREC_SPLIT then computes the GEMMs with fp32-accurate
+                              weights (trained fp32 checkpoints); NULL when the weights are bf16 */
 } NcaModelDesc;
+
+typedef enum NcaHeadKind { NCA_HEAD_LINEAR = 0, NCA_HEAD_L2 = 1 } NcaHeadKind;
 
 /* A batch of instances (board x trial rows of the reference's flattened batch,
  * src/nca/rollout.py:144-150).  Instance `inst` uses clamp row inst_row[inst], or inst / trials

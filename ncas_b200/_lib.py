@@ -32,6 +32,7 @@ PREC_BF16, PREC_SPLIT = 0, 1
 FIRE_MASK, FIRE_PHILOX, FIRE_ADAPTIVE_PHILOX, FIRE_ADAPTIVE_UNIFORM = 0, 1, 2, 3
 FIRE_THRESHOLD_PHILOX, FIRE_THRESHOLD_UNIFORM = 4, 5
 NOISE_NONE, NOISE_PHILOX, NOISE_EXTERNAL = 0, 1, 2
+HEAD_LINEAR, HEAD_L2 = 0, 1
 
 
 class NcaModelDesc(C.Structure):
@@ -52,6 +53,9 @@ class NcaModelDesc(C.Structure):
         ("weights", C.c_void_p),
         ("b1", C.c_void_p),
         ("b2", C.c_void_p),
+        ("head_kind", C.c_int32),
+        ("pad", C.c_float * 64),
+        ("weights_lo", C.c_void_p),
     ]
 
 

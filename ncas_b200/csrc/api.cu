@@ -160,14 +160,15 @@ __global__ void state_store_kernel(const float* master, int C, long long total, 
 
 // ------------------------------------------------------------------------------- readout
 struct ReadoutArgs {
-  int C, hw, n_inst, c_out, out_off, n_out;
+  int C, hw, n_inst, c_out, out_off, n_out, head_kind;
   float head_w[16][16];
   float head_b[16];
   int out_tokens[16];
 };
 
-// One block per instance.  Scores of the mlp head on the readout slice, argmax (first maximum,
-// as torch.argmax), max-softmax confidence clamped to [0, 1] (src/nca/model.py:596-633).
+// One block per instance.  head_readout of every cell (argmax as torch.argmax, the head's
+// confidence clamped to [0, 1], src/nca/model.py:596-633), the decoded token (given cells show
+// their input, src/nca/rollout.py:74-82), the board confidence and, with targets, the accuracy.
 __global__ void readout_kernel(const float* master, NcaBatchDesc b, ReadoutArgs R, uint8_t* pred,
                                float* cell_conf, float* board_conf, const uint8_t* targets,
                                float* cell_acc, uint8_t* exact) {
@@ -179,24 +180,19 @@ __global__ void readout_kernel(const float* master, NcaBatchDesc b, ReadoutArgs 
     const long long t = g >> 7;
     const int m = (int)(g & 127);
     float xo[16];
-    for (int c = 0; c < R.c_out; ++c) {
-      const int cc = R.out_off + c;
-      xo[c] = master[((t * (R.C / 4) + (cc >> 2)) * kTileM + m) * 4 + (cc & 3)];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      xo[c] = 0.f;
+      if (c < R.c_out) {
+        const int cc = R.out_off + c;
+        xo[c] = master[((t * (R.C / 4) + (cc >> 2)) * kTileM + m) * 4 + (cc & 3)];
+      }
     }
-    float best = -3.402823466e38f;
-    int arg = 0;
-    float sc[16];
-    for (int o = 0; o < R.n_out; ++o) {
-      float a = R.head_b[o];
-      for (int c = 0; c < R.c_out; ++c) a = fmaf(R.head_w[o][c], xo[c], a);
-      sc[o] = a;
-      if (a > best || o == 0) { best = a; arg = o; }
-    }
-    float den = 0.f;
-    for (int o = 0; o < R.n_out; ++o) den += expf(sc[o] - best);
-    const float conf = fminf(fmaxf(1.f / den, 0.f), 1.f);
+    float conf;
+    int arg;
+    head_readout(R.head_kind, R.n_out, R.c_out, R.head_w, R.head_b, xo, conf, arg);
     conf_sum += conf;
-    const long long bp = (long long)row * R.hw + p;
+  const long long bp = (long long)row * R.hw + p;
     const bool gv = b.given[bp] != 0;
     const int tok = gv ? (int)b.inputs[bp] : R.out_tokens[arg];
     if (pred) pred[(long long)inst * R.hw + p] = (uint8_t)tok;
@@ -515,6 +511,9 @@ int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaState* st,
   memcpy(A.head_w, m->head_w, sizeof(A.head_w));
   memcpy(A.head_b, m->head_b, sizeof(A.head_b));
   A.wimg = reinterpret_cast<const uint8_t*>(m->weights);
+  A.wimg_lo = (st->precision == NCA_PREC_SPLIT) ? reinterpret_cast<const uint8_t*>(m->weights_lo) : nullptr;
+  A.head_kind = m->head_kind;
+  memcpy(A.pad, m->pad, sizeof(A.pad));
   A.b1 = m->b1;
   A.b2 = m->b2;
   A.given = b->given;
@@ -547,10 +546,10 @@ int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaState* st,
   A.timeout_ns = (unsigned long long)(timeout_ms > 0 ? timeout_ms : 10000) * 1000000ull;
 
   int stages = 2;
-  int smem = SmemLayout<Cfg>(stages, A.win_cells).total + 1024;
+  int smem = SmemLayout<Cfg>(stages, A.win_cells, A.wimg_lo != nullptr).total + 1024;
   if (smem > kMaxSmem) {
     stages = 1;
-    smem = SmemLayout<Cfg>(stages, A.win_cells).total + 1024;
+    smem = SmemLayout<Cfg>(stages, A.win_cells, A.wimg_lo != nullptr).total + 1024;
   }
   if (smem > kMaxSmem) return NCA_ERR_UNSUPPORTED;
   A.stages = stages;
@@ -588,6 +587,8 @@ bool model_ok(const NcaModelDesc* m) {
       m->out_offset + m->c_out > m->channels)
     return false;
   if (m->n_out < 1 || m->n_out > NCA_B200_MAX_OUT) return false;
+  if (m->head_kind != NCA_HEAD_LINEAR && m->head_kind != NCA_HEAD_L2) return false;
+  if (m->channels > 64) return false;
   return true;
 }
 
@@ -746,20 +747,21 @@ int32_t nca_b200_run_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaStat
   if (fire->noise_mode == NCA_NOISE_EXTERNAL && (!fire->noise || n_steps != 1)) return NCA_ERR_INVALID;
   const bool noise = fire->noise_mode != NCA_NOISE_NONE;
   auto launch = [&](int32_t n, const NcaFireDesc* f) -> int32_t {
-    if (C == 32 && HD == 128) {
-      if (noise)
-        return split ? launch_steps<StepCfg<32, 128, true, true>>(m, b, st, n, f, ctrl, timeout_ms, s)
-                     : launch_steps<StepCfg<32, 128, false, true>>(m, b, st, n, f, ctrl, timeout_ms, s);
-      return split ? launch_steps<StepCfg<32, 128, true>>(m, b, st, n, f, ctrl, timeout_ms, s)
-                   : launch_steps<StepCfg<32, 128, false>>(m, b, st, n, f, ctrl, timeout_ms, s);
-    }
-    if (C == 64 && HD == 256) {
-      if (noise)
-        return split ? launch_steps<StepCfg<64, 256, true, true>>(m, b, st, n, f, ctrl, timeout_ms, s)
-                     : launch_steps<StepCfg<64, 256, false, true>>(m, b, st, n, f, ctrl, timeout_ms, s);
-      return split ? launch_steps<StepCfg<64, 256, true>>(m, b, st, n, f, ctrl, timeout_ms, s)
-                   : launch_steps<StepCfg<64, 256, false>>(m, b, st, n, f, ctrl, timeout_ms, s);
-    }
+#define NCA_LAUNCH(CC, HH)                                                                          \
+  if (C == CC && HD == HH) {                                                                        \
+    if (noise)                                                                                      \
+      return split ? launch_steps<StepCfg<CC, HH, true, true>>(m, b, st, n, f, ctrl, timeout_ms, s)  \
+                   : launch_steps<StepCfg<CC, HH, false, true>>(m, b, st, n, f, ctrl, timeout_ms, s); \
+    return split ? launch_steps<StepCfg<CC, HH, true>>(m, b, st, n, f, ctrl, timeout_ms, s)          \
+                 : launch_steps<StepCfg<CC, HH, false>>(m, b, st, n, f, ctrl, timeout_ms, s);        \
+  }
+    // the benchmark models (32, 128), (64, 256) and the reference's maze presets (16, 128),
+    // (32, 256) (maze_ood, maze_hard: src/nca/model.py:656-700)
+    NCA_LAUNCH(32, 128)
+    NCA_LAUNCH(64, 256)
+    NCA_LAUNCH(16, 128)
+    NCA_LAUNCH(32, 256)
+#undef NCA_LAUNCH
     return NCA_ERR_UNSUPPORTED;
   };
   if (st->clamped) return launch(n_steps, fire);
@@ -795,6 +797,7 @@ int32_t nca_b200_readout(const NcaModelDesc* m, const NcaBatchDesc* b, const Nca
   R.c_out = m->c_out;
   R.out_off = m->out_offset;
   R.n_out = m->n_out;
+  R.head_kind = m->head_kind;
   memcpy(R.head_w, m->head_w, sizeof(R.head_w));
   memcpy(R.head_b, m->head_b, sizeof(R.head_b));
   memcpy(R.out_tokens, m->out_tokens, sizeof(R.out_tokens));

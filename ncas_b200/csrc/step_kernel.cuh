@@ -98,6 +98,8 @@ struct StepArgs {
   float head_w[16][16];
   float head_b[16];
   const uint8_t* wimg;
+  const uint8_t* wimg_lo;  // residual image (split mode with fp32 weights) or null
+  int head_kind;
   const float* b1;
   const float* b2;
   const uint8_t* given;
@@ -125,11 +127,13 @@ struct StepArgs {
 // Shared-memory layout (offsets from a 1024-byte aligned base).
 template <class Cfg>
 struct SmemLayout {
-  int w1, w2, win, b1, b2, flags, bars, misc, total;
-  __host__ __device__ SmemLayout(int stages, int win_cells) {
+  int w1, w2, w1lo, w2lo, win, b1, b2, flags, bars, misc, total;
+  __host__ __device__ SmemLayout(int stages, int win_cells, bool lo) {
     w1 = 0;
     w2 = w1 + Cfg::W1_BYTES;
-    win = (w2 + Cfg::W2_BYTES + 1023) & ~1023;
+    w1lo = w2 + Cfg::W2_BYTES;  // the residual image, when present, follows (same layout)
+    w2lo = w1lo + Cfg::W1_BYTES;
+    win = ((lo ? w2lo + Cfg::W2_BYTES : w1lo) + 1023) & ~1023;
     b1 = (win + stages * (win_cells + 1) * Cfg::ROWB + 15) & ~15;  // + the padding cell
     b2 = b1 + Cfg::HD * 4;
     flags = b2 + Cfg::C * 4;
@@ -226,13 +230,59 @@ __device__ __forceinline__ void fixed_taps4(float a, float b, float c, float d, 
   lap = s * 0.0625f;
 }
 
-// Adaptive firing of one cell at step s on the reference's confidence (src/nca/model.py:624-629,
-// max softmax of the head scores of the cell's fp32 state): the continuous rule
-// p = scale * (1 - conf) + bias, or the reference's threshold rule (src/nca/model.py:566-593)
-// p = p_low for confident cells (conf > tau, or given cells when given_confident), else p_fire;
-// fire when u < p with u from Philox or from the caller.
+// Readout of one cell from its readout slice xs[0 .. c_out) (src/nca/model.py:596-633):
+// kind 0 (head "mlp"): scores head_w x + head_b, confidence the max softmax;
+// kind 1 (head "l2"): rows of head_w are the output-token embeddings e_o, score
+// 1 / (1 + sqrt(|x - e_o|^2 + 1e-8)), confidence the best score.  arg is the first best token
+// (torch.argmax).  The loops run to the compile-time maximum with uniform exits, so the slice
+// stays in registers.
+__device__ __forceinline__ void head_readout(int kind, int n_out, int c_out, const float (&hw)[16][16],
+                                             const float (&hb)[16], const float (&xs)[16],
+                                             float& conf, int& arg) {
+  auto score = [&](int o) {
+    if (kind == 1) {
+      float d2 = 0.f;
+#pragma unroll
+      for (int c = 0; c < 16; ++c)
+        if (c < c_out) {
+          const float d = xs[c] - hw[o][c];
+          d2 = fmaf(d, d, d2);
+        }
+      return 1.f / (1.f + sqrtf(d2 + 1e-8f));
+    }
+    float a = hb[o];
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+      if (c < c_out) a = fmaf(hw[o][c], xs[c], a);
+    return a;
+  };
+  float best = -3.402823466e38f;
+  int a = 0;
+#pragma unroll
+  for (int o = 0; o < 16; ++o) {
+    if (o >= n_out) break;
+    const float sc = score(o);
+    if (sc > best || o == 0) { best = sc; a = o; }
+  }
+  arg = a;
+  if (kind == 1) {
+    conf = fminf(fmaxf(best, 0.f), 1.f);
+    return;
+  }
+  float den = 0.f;
+#pragma unroll
+  for (int o = 0; o < 16; ++o) {
+    if (o >= n_out) break;
+    den += expf(score(o) - best);
+  }
+  conf = fminf(fmaxf(1.f / den, 0.f), 1.f);
+}
+
+// Adaptive firing of one cell at step s on the reference's confidence (head_readout of the
+// cell's fp32 state): the continuous rule p = scale * (1 - conf) + bias, or the reference's
+// threshold rule (src/nca/model.py:566-593) p = p_low for confident cells (conf > tau, or given
+// cells when given_confident), else p_fire; fire when u < p with u from Philox or the caller.
 // Read from the fp32 state of the step's input buffer (complete since the last grid barrier).
-// The loops run to the compile-time maximum with uniform exits, so the slice stays in registers.
 template <class Cfg>
 __device__ __forceinline__ bool adaptive_fire(const StepArgs& A, int s, long long t, int m, int inst,
                                               int p, bool given) {
@@ -246,24 +296,9 @@ __device__ __forceinline__ bool adaptive_fire(const StepArgs& A, int s, long lon
       xs[c] = __ldg(xin + ((((t * (Cfg::C / 4) + (cc >> 2)) << 7) + m) * 4 + (cc & 3)));
     }
   }
-  // two passes over the head (max, then the softmax denominator) recompute the scores instead
-  // of keeping them
-  auto score = [&](int o) {
-    float a = A.head_b[o];
-#pragma unroll
-    for (int c = 0; c < 16; ++c)
-      if (c < A.c_out) a = fmaf(A.head_w[o][c], xs[c], a);
-    return a;
-  };
-  float mx = -3.402823466e38f;
-#pragma unroll
-  for (int o = 0; o < 16; ++o)
-    if (o < A.n_out) mx = fmaxf(mx, score(o));
-  float den = 0.f;
-#pragma unroll
-  for (int o = 0; o < 16; ++o)
-    if (o < A.n_out) den += expf(score(o) - mx);
-  const float conf = fminf(fmaxf(1.f / den, 0.f), 1.f);
+  float conf;
+  int arg;
+  head_readout(A.head_kind, A.n_out, A.c_out, A.head_w, A.head_b, xs, conf, arg);
   float prob;
   if (A.fire_mode >= 4)  // threshold rule: confident cells fire at p_low
     prob = (conf > A.tau || (given && A.given_confident)) ? A.p_low : A.p_fire;
@@ -280,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
   using namespace nca;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  const SmemLayout<Cfg> L(A.stages, A.win_cells);
+  const SmemLayout<Cfg> L(A.stages, A.win_cells, A.wimg_lo != nullptr);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L.misc);
   int* abort_flag = reinterpret_cast<int*>(smem + L.misc + 8);
@@ -368,6 +403,10 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
       const uint64_t d1 = umma_desc_sw128(w1);
       const uint64_t d2 = umma_desc_sw128(w2);
       const uint32_t id2 = idesc_bf16_f32(kTileM, Cfg::C);
+      // split mode with fp32 weights: the residual image adds z_hi * W_lo (and h_hi * W2_lo)
+      const bool wlo = Cfg::SPLIT && A.wimg_lo != nullptr;
+      const uint64_t d1lo = umma_desc_sw128(smem_u32(smem + L.w1lo));
+      const uint64_t d2lo = umma_desc_sw128(smem_u32(smem + L.w2lo));
       long long it = 0;
       for (int s = 0; ok && s < A.n_steps; ++s) {
         for (long long t = blockIdx.x; ok && t < A.n_tiles; t += grid, ++it) {
@@ -391,6 +430,9 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
               for (int part = 0; part < Cfg::ZPARTS; ++part)
                 umma_bf16_ts(tmem + Cfg::ACC_COL + nh * (Cfg::HD / 2), zcol + part * (Cfg::P / 2) + kk * 8,
                              desc_add(d1, boff), id1, (kk | part) != 0);
+              if (Cfg::SPLIT && wlo)
+                umma_bf16_ts(tmem + Cfg::ACC_COL + nh * (Cfg::HD / 2), zcol + kk * 8, desc_add(d1lo, boff),
+                             id1, 1u);
             }
             if (Cfg::H_IN_ACC) umma_commit(&bars[nh == 0 ? BAR_ACC_FULL : BAR_ACC_FULL_B]);
           }
@@ -417,6 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
                 for (int part = 0; part < Cfg::ZPARTS; ++part)
                   umma_bf16_ts(tmem + Cfg::ACC2_COL, zcol + part * (Cfg::HD / 2) + kk * 8, desc_add(d2, boff),
                                id2, (kk | part) != 0);
+                if (wlo) umma_bf16_ts(tmem + Cfg::ACC2_COL, zcol + kk * 8, desc_add(d2lo, boff), id2, 1u);
               }
             }
           }
@@ -437,12 +480,19 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
   } else if (!skip && warp == 1) {
     // ---------------------------------------------------------------- loader
     if (lane == 0) {
-      mbar_arrive_expect_tx(&bars[BAR_WEIGHTS], Cfg::W1_BYTES + Cfg::W2_BYTES);
-      const uint32_t dst = smem_u32(smem + L.w1);
       const int tot = Cfg::W1_BYTES + Cfg::W2_BYTES;   // w1 and w2 are contiguous in smem
+      mbar_arrive_expect_tx(&bars[BAR_WEIGHTS], A.wimg_lo ? 2 * tot : tot);
+      const uint32_t dst = smem_u32(smem + L.w1);
       for (int off = 0; off < tot; off += 16384) {
         const int n = (tot - off) < 16384 ? (tot - off) : 16384;
         bulk_g2s(dst + off, A.wimg + off, n, &bars[BAR_WEIGHTS]);
+      }
+      if (A.wimg_lo) {
+        const uint32_t dlo = smem_u32(smem + L.w1lo);
+        for (int off = 0; off < tot; off += 16384) {
+          const int n = (tot - off) < 16384 ? (tot - off) : 16384;
+          bulk_g2s(dlo + off, A.wimg_lo + off, n, &bars[BAR_WEIGHTS]);
+        }
       }
     }
     __syncwarp();
@@ -783,8 +833,11 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         uint32_t r[CH];
         if constexpr (CH == 32) {
           tmem_ld32(abase + (Cfg::ACC2_COL - Cfg::ACC_COL) + half * CH, r);
-        } else {
+        } else if constexpr (CH == 16) {
           tmem_ld16(abase + (Cfg::ACC2_COL - Cfg::ACC_COL) + half * CH, *reinterpret_cast<uint32_t(*)[16]>(r));
+        } else {
+          static_assert(CH == 8, "channels per epilogue thread");
+          tmem_ld8(abase + (Cfg::ACC2_COL - Cfg::ACC_COL) + half * CH, *reinterpret_cast<uint32_t(*)[8]>(r));
         }
         tc_wait_ld_regs(r);
         tc_fence_before();

@@ -27,6 +27,13 @@ from .model import FIXED_TAPS, check_supported
 DEFAULT_TIMEOUT_MS = int(os.environ.get("NCA_B200_TIMEOUT_MS", "20000"))
 
 
+def _bf16(a: np.ndarray) -> np.ndarray:
+    """Nearest bf16 values (ties to even) of an fp32 array, as fp32."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
 def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
@@ -110,8 +117,13 @@ class B200Engine:
         self.b1 = model.update.fc1.bias.detach().float().contiguous().to(self.device)
         self.b2 = model.update.fc2.bias.detach().float().contiguous().to(self.device)
         taps = model.perceive.weight.detach().float().reshape(4, 9).cpu().numpy()
-        hw_ = model.head.weight.detach().float().reshape(len(cfg.output_tokens), cfg.c_out).cpu().numpy()
-        hb = model.head.bias.detach().float().cpu().numpy()
+        n_out = len(cfg.output_tokens)
+        if cfg.head == "l2":  # rows are the output-token embeddings (src/nca/model.py:600-602)
+            hw_ = model.out_embed.detach().float().reshape(n_out, cfg.c_out).cpu().numpy()
+            hb = np.zeros(n_out, np.float32)
+        else:
+            hw_ = model.head.weight.detach().float().reshape(n_out, cfg.c_out).cpu().numpy()
+            hb = model.head.bias.detach().float().cpu().numpy()
         d = L.NcaModelDesc()
         d.channels, d.perception, d.hidden = C_, P, Hd
         d.c_in, d.in_offset, d.c_out, d.out_offset = cfg.c_in, cfg.in_offset, cfg.c_out, cfg.out_offset
@@ -125,6 +137,25 @@ class B200Engine:
             d.out_tokens[o] = int(cfg.output_tokens[o])
             for c in range(cfg.c_out):
                 d.head_w[o][c] = float(hw_[o, c])
+        d.head_kind = L.HEAD_L2 if cfg.head == "l2" else L.HEAD_LINEAR
+        pad = getattr(model, "pad_vec", None)
+        if pad is not None:
+            pv = pad.detach().float().cpu().numpy()
+            for c in range(C_):
+                d.pad[c] = float(pv[c])
+        # Split mode with weights that are not bf16 values (trained checkpoints): the image of the
+        # residual w - bf16(w) makes the GEMMs fp32-accurate in the weights too.
+        self.wimg_lo = None
+        if precision == "split":
+            r1 = w1h - _bf16(w1h)
+            r2 = w2h - _bf16(w2h)
+            if np.any(r1) or np.any(r2):
+                lo = np.zeros(int(nbytes.value), dtype=np.uint8)
+                L.check(lib.nca_b200_pack_weights(np.ascontiguousarray(r1).ctypes.data,
+                                                  np.ascontiguousarray(r2).ctypes.data, C_, P, Hd,
+                                                  lo.ctypes.data), "nca_b200_pack_weights")
+                self.wimg_lo = torch.from_numpy(lo).to(self.device)
+                d.weights_lo = self.wimg_lo.data_ptr()
         d.weights = self.wimg.data_ptr()
         d.b1 = self.b1.data_ptr()
         d.b2 = self.b2.data_ptr()

@@ -97,26 +97,46 @@ class NCAConfig:
         return cls(**d)
 
 
+# (channels, hidden) instances of the step kernel: the benchmark models and the reference's
+# maze presets (maze_ood 16/128, maze_hard 32/256)
+KERNEL_SHAPES = ((32, 128), (64, 256), (16, 128), (32, 256))
+
+# The reference's maze presets (src/nca/model.py:656-700), the ones whose cell rule the kernels
+# implement: learned 4-head 3x3 perception, wall padding, MLP update, l2 head.
+PRESETS: dict[str, dict] = {
+    "maze_ood": dict(vocab_size=4, channels=16, c_in=16, c_out=2, output_tokens=(0, 1),
+                     perception="kernels", hidden_from_perception=True, heads=4, padding="wall",
+                     wall_token=2, update="mlp", expansion=2, norm_groups=0, sigma_init=0.15,
+                     fire_rate=0.8, head="l2", embedding="onehot"),
+    "maze_hard": dict(vocab_size=5, channels=32, c_in=32, c_out=3, output_tokens=(0, 1),
+                      perception="kernels", hidden_from_perception=True, heads=4, padding="wall",
+                      wall_token=2, update="mlp", expansion=2, norm_groups=0, sigma_init=0.25,
+                      fire_rate=0.8, head="l2", embedding="onehot"),
+}
+
+
 def unsupported_reason(cfg) -> str | None:
     """Why the B200 kernels cannot run this cell rule (None when they can).  Accepts the
     reference's NCAConfig as well as ours."""
     if cfg.perception != "kernels" or cfg.heads != 4:
         return f"perception={cfg.perception!r} heads={cfg.heads} (needs 4-head 'kernels')"
-    if cfg.padding != "zero":
-        return f"padding={cfg.padding!r} (needs 'zero')"
+    if cfg.padding not in ("zero", "wall"):
+        return f"padding={cfg.padding!r} (needs 'zero' or 'wall')"
     if cfg.update != "mlp":
         return f"update={cfg.update!r} (needs 'mlp')"
     if cfg.norm_groups:
         return "group normalisation"
     if cfg.time_steps or cfg.c_task or cfg.n_tasks:
         return "step or task embeddings"
-    if cfg.head != "mlp":
-        return f"head={cfg.head!r} (needs 'mlp')"
+    if cfg.head not in ("mlp", "l2"):
+        return f"head={cfg.head!r} (needs 'mlp' or 'l2')"
+    if cfg.embedding != "onehot":
+        return f"embedding={cfg.embedding!r} (needs 'onehot')"
     if getattr(cfg, "project_update", False) or getattr(cfg, "noise_after_norm", False):
         return "public-code update switches"
     hid = cfg.expansion * (cfg.heads * cfg.channels if cfg.hidden_from_perception else cfg.channels)
-    if (cfg.channels, hid) not in ((32, 128), (64, 256)):
-        return f"channels={cfg.channels}, hidden={hid} (kernels exist for 32/128 and 64/256)"
+    if (cfg.channels, hid) not in KERNEL_SHAPES:
+        return f"channels={cfg.channels}, hidden={hid} (kernels exist for {sorted(KERNEL_SHAPES)})"
     if cfg.c_out > 16 or len(cfg.output_tokens) > 16:
         return "more than 16 readout channels or tokens"
     return None
@@ -159,6 +179,16 @@ class NCA(nn.Module):
         self.cfg = cfg
         self.precision = precision
         self.register_buffer("embed", make_embeddings(cfg.vocab_size, cfg.c_in, cfg.embedding))
+        # embeddings of the predictable tokens in the output slice (l2 head), and the state of
+        # the cells outside the board (wall padding: the wall token's embedding in the input
+        # slice), as the reference's buffers (src/nca/model.py:314-325)
+        if cfg.head in ("l2", "cosine"):
+            lo = cfg.out_offset - cfg.in_offset
+            self.register_buffer("out_embed", self.embed[list(cfg.output_tokens)][:, lo : lo + cfg.c_out].clone())
+        pad_vec = torch.zeros(cfg.channels)
+        if cfg.padding == "wall":
+            pad_vec[cfg.in_slice] = self.embed[cfg.wall_token]
+        self.register_buffer("pad_vec", pad_vec)
         self.perceive = KernelPerception(cfg.channels, cfg.heads)
         self.update = MLPUpdate(cfg.heads * cfg.channels, cfg.channels, cfg.hidden)
         if cfg.head == "mlp":
@@ -231,9 +261,23 @@ class NCA(nn.Module):
 
 
 def build_model(preset: str | None = None, precision: str = "bf16", **overrides) -> NCA:
-    """`build_model(None, **cfg_fields)` as src/nca/model.py:766-771 (no presets are
-    implemented by the kernels; the benchmark models come from `ncas_b200.configs`)."""
-    if preset is not None:
-        raise ValueError("reference presets need padding/heads the b200 kernels do not implement")
-    overrides["output_tokens"] = tuple(overrides["output_tokens"])
-    return NCA(NCAConfig(**overrides), precision=precision)
+    """`build_model("maze_hard")` or `build_model(None, **cfg_fields)` as src/nca/model.py:766-771;
+    the presets whose cell rule the kernels implement are in PRESETS."""
+    if preset is not None and preset not in PRESETS:
+        raise ValueError(f"preset {preset!r} needs a cell rule the b200 kernels do not implement "
+                         f"(available: {sorted(PRESETS)})")
+    d = dict(PRESETS[preset]) if preset else {}
+    d.update(overrides)
+    d["output_tokens"] = tuple(d["output_tokens"])
+    return NCA(NCAConfig(**d), precision=precision)
+
+
+def load_model(path, device=None, precision: str = "bf16"):
+    """A trained checkpoint (the reference's final.pt: model_config, EMA weights, run config) as
+    nca.train.load_model (src/nca/train.py:694-701): returns (model, run config)."""
+    ck = torch.load(path, map_location="cpu", weights_only=False)
+    model = NCA(NCAConfig.from_dict(dict(ck["model_config"])), precision=precision)
+    model.load_state_dict(ck["model"])
+    if device is not None:
+        model = model.to(device)
+    return model.eval(), ck.get("config", {})

@@ -17,6 +17,7 @@ Host-side numpy only: board generation and scoring are not on the timed path.
 
 from __future__ import annotations
 
+import heapq
 from collections import deque
 from dataclasses import dataclass, field
 
@@ -94,6 +95,15 @@ class Task:
 class MazeTask(Task):
     name = "maze"
     vocab_size = 5
+    output_tokens = (EMPTY, PATH)
+
+
+class MazeOODTask(Task):
+    """Maze-OOD's 4-token vocabulary (src/nca/tasks/maze.py:71, 874-875): both endpoints are
+    token 3."""
+
+    name = "maze_ood"
+    vocab_size = 4
     output_tokens = (EMPTY, PATH)
 
 
@@ -182,6 +192,69 @@ def shortest_path(passable: np.ndarray, src, dst) -> list[tuple[int, int]]:
     return path[::-1]
 
 
+_MOVES = ((-1, 0), (1, 0), (0, -1), (0, 1))  # up, down, left, right
+
+
+def _walk_back(parent: dict, src, dst) -> list[tuple[int, int]]:
+    path = [dst]
+    while path[-1] != src:
+        path.append(parent[path[-1]])
+    return path[::-1]
+
+
+def bfs_parent_path(passable: np.ndarray, src, dst) -> list[tuple[int, int]]:
+    """Shortest path by breadth-first search with parents set on first discovery, neighbours
+    tried up, down, left, right, stopping when dst is discovered (the `bfs` targets of
+    src/nca/tasks/maze.py:130-160)."""
+    H, W = passable.shape
+    src, dst = tuple(src), tuple(dst)
+    parent = {src: src}
+    q = deque([src])
+    while q and dst not in parent:
+        i, j = q.popleft()
+        for di, dj in _MOVES:
+            nb = (i + di, j + dj)
+            if 0 <= nb[0] < H and 0 <= nb[1] < W and passable[nb] and nb not in parent:
+                parent[nb] = (i, j)
+                if nb == dst:
+                    break
+                q.append(nb)
+    assert dst in parent, "unreachable"
+    return _walk_back(parent, src, dst)
+
+
+def astar_path(passable: np.ndarray, src, dst) -> list[tuple[int, int]]:
+    """Shortest path by A* with the Manhattan heuristic (the `astar` targets of
+    src/nca/tasks/maze.py:187-230): the open cell with the smallest f = g + h is expanded
+    first, ties broken by the smaller h, then by insertion order; neighbours are tried up, down,
+    left, right, and a cell's parent is replaced only by a strictly shorter route."""
+    H, W = passable.shape
+    src, dst = tuple(src), tuple(dst)
+    h = lambda c: abs(c[0] - dst[0]) + abs(c[1] - dst[1])  # noqa: E731
+    g = {src: 0}
+    parent = {src: src}
+    closed = set()
+    order = 0
+    heap = [(h(src), h(src), order, src)]
+    while heap:
+        _, _, _, c = heapq.heappop(heap)
+        if c in closed:
+            continue
+        if c == dst:
+            return _walk_back(parent, src, dst)
+        closed.add(c)
+        for di, dj in _MOVES:
+            nb = (c[0] + di, c[1] + dj)
+            if not (0 <= nb[0] < H and 0 <= nb[1] < W) or not passable[nb] or nb in closed:
+                continue
+            if nb not in g or g[c] + 1 < g[nb]:
+                g[nb] = g[c] + 1
+                parent[nb] = c
+                order += 1
+                heapq.heappush(heap, (g[nb] + h(nb), h(nb), order, nb))
+    raise AssertionError("unreachable")
+
+
 def _with_path(grid: np.ndarray, path, start_tok: int, goal_tok: int) -> np.ndarray:
     t = grid.copy()
     for i, j in path[1:-1]:
@@ -198,10 +271,12 @@ def _goal_second(inputs: np.ndarray, target: np.ndarray, a, b):
     target[first], target[second] = START, GOAL
 
 
-def perfect_maze(size: int, rng: np.random.Generator) -> tuple[np.ndarray, np.ndarray]:
+def perfect_maze(size: int, rng: np.random.Generator, goal: bool = True) -> tuple[np.ndarray, np.ndarray]:
     """A Maze-OOD style maze of odd `size` (draws as src/nca/tasks/maze.py:364-384): a perfect
     maze on the ((size-1)/2)^2 lattice and two distinct random corridor cells as endpoints.
-    Returns (inputs, target) uint8 with tokens EMPTY/PATH/WALL/START/GOAL."""
+    Returns (inputs, target) uint8 with tokens EMPTY/PATH/WALL/START/GOAL; with goal=False both
+    endpoints keep the START (the reference's Maze-OOD ENDPOINT) token, the 4-token vocabulary
+    of the maze_ood preset."""
     if size < 5 or size % 2 == 0:
         raise ValueError(f"size must be odd and >= 5, got {size}")
     grid = carve_tree((size - 1) // 2, rng)
@@ -211,7 +286,11 @@ def perfect_maze(size: int, rng: np.random.Generator) -> tuple[np.ndarray, np.nd
     path = shortest_path(grid != WALL, a, b)
     target = _with_path(grid, path, START, GOAL)
     inputs = grid.copy()
-    _goal_second(inputs, target, a, b)
+    if goal:
+        _goal_second(inputs, target, a, b)
+    else:
+        inputs[a], inputs[b] = START, START
+        target[a], target[b] = START, START
     return inputs, target
 
 
@@ -221,11 +300,14 @@ def hard_maze(
     min_path_len: int = 60,
     extra_openings: float = 0.10,
     max_tries: int = 1000,
+    targets: str = "astar",
 ) -> tuple[np.ndarray, np.ndarray]:
     """A maze with loops (draws as src/nca/tasks/maze.py:387-445): a perfect (size+1)^2 maze,
     a fraction `extra_openings` of the removable interior walls opened, cropped to size x size;
     start = a random corridor cell, goal = a random corridor cell at BFS distance
-    >= min_path_len - 1.  The target marks one shortest path (BFS walk-back tie-break)."""
+    >= min_path_len - 1.  The target marks one shortest path, chosen as the reference's Maze-Hard
+    task does: `targets` 'astar' (its default) or 'bfs'."""
+    path_fn = {"astar": astar_path, "bfs": bfs_parent_path}[targets]
     if size % 2:
         raise ValueError("size must be even")
     k = size // 2
@@ -251,18 +333,18 @@ def hard_maze(
             if len(far) == 0:
                 continue
             dst = tuple(int(v) for v in far[rng.integers(len(far))])
-            target = _with_path(grid, shortest_path(passable, src, dst), START, GOAL)
+            target = _with_path(grid, path_fn(passable, src, dst), START, GOAL)
             inputs = grid.copy()
             inputs[src], inputs[dst] = START, GOAL
             return inputs, target
     raise RuntimeError("no maze satisfied min_path_len")
 
 
-def maze_boards(n: int, size: int, seed: int, hard: bool = False, **kw) -> Boards:
+def maze_boards(n: int, size: int, seed: int, hard: bool = False, goal: bool = True, **kw) -> Boards:
     rng = np.random.default_rng(seed)
     ins, tgs = [], []
     for _ in range(n):
-        inp, tgt = hard_maze(size, rng, **kw) if hard else perfect_maze(size, rng)
+        inp, tgt = hard_maze(size, rng, **kw) if hard else perfect_maze(size, rng, goal=goal)
         ins.append(inp)
         tgs.append(tgt)
     inputs = np.stack(ins).astype(np.int64)

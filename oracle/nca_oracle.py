@@ -19,14 +19,17 @@ F32 = np.float32
 
 
 # ---------------------------------------------------------------------------- the cell rule
-def perceive_nhwc(x: np.ndarray, taps: np.ndarray) -> np.ndarray:
-    """KernelPerception with zero padding on a channels-last state: x (B, H, W, C) ->
-    z (B, H, W, heads*C), head-major z[..., k*C + c] = sum_n taps[k, n] * x[shifted n, c]
-    (src/nca/model.py:140-152, 175-178; taps summed in row-major order n = 0..8)."""
+def perceive_nhwc(x: np.ndarray, taps: np.ndarray, pad=None) -> np.ndarray:
+    """KernelPerception on a channels-last state: x (B, H, W, C) -> z (B, H, W, heads*C),
+    head-major z[..., k*C + c] = sum_n taps[k, n] * x[shifted n, c] (src/nca/model.py:175-178;
+    taps summed in row-major order n = 0..8).  The border is zero, or the vector `pad` (C,) for
+    wall padding (src/nca/model.py:140-152)."""
     B, H, W, C = x.shape
     heads = taps.shape[0]
     t = taps.reshape(heads, 9).astype(F32)
     xp = np.zeros((B, H + 2, W + 2, C), F32)
+    if pad is not None:
+        xp[:] = np.asarray(pad, F32)
     xp[:, 1:-1, 1:-1] = x
     z = np.zeros((B, H, W, heads, C), F32)
     tmp = np.empty((B, H, W, C), F32)
@@ -40,9 +43,9 @@ def perceive_nhwc(x: np.ndarray, taps: np.ndarray) -> np.ndarray:
     return z.reshape(B, H, W, heads * C)
 
 
-def perceive(x: np.ndarray, taps: np.ndarray) -> np.ndarray:
+def perceive(x: np.ndarray, taps: np.ndarray, pad=None) -> np.ndarray:
     """perceive_nhwc on the reference's (B, C, H, W) layout: z (B, heads*C, H, W)."""
-    z = perceive_nhwc(np.ascontiguousarray(x.transpose(0, 2, 3, 1)), taps)
+    z = perceive_nhwc(np.ascontiguousarray(x.transpose(0, 2, 3, 1)), taps, pad)
     return np.ascontiguousarray(z.transpose(0, 3, 1, 2))
 
 
@@ -79,7 +82,7 @@ def step_nhwc(x, given, clamp_nhwc, fire, p: dict, noise=None) -> np.ndarray:
     fire (B, H, W) {0, 1}, noise (B, H, W, C) or None.  x' = x + fire * dx (+ noise), then the
     clamp."""
     B, H, W, C = x.shape
-    z = perceive_nhwc(x, p["taps"])
+    z = perceive_nhwc(x, p["taps"], p.get("pad"))
     dx = mlp_rows(z.reshape(B * H * W, -1), p["w1"], p["b1"], p["w2"], p["b2"]).reshape(B, H, W, C)
     np.multiply(dx, fire.reshape(B, H, W, 1).astype(F32), out=dx)
     np.add(dx, x, out=dx)
@@ -99,8 +102,14 @@ def step(x, given4, clamp, fire, p: dict) -> np.ndarray:
 
 
 def scores(x, p: dict) -> np.ndarray:
-    """mlp head on the readout slice (src/nca/model.py:596-609): (B, n_out, H, W)."""
+    """Head scores on the readout slice (src/nca/model.py:596-609): (B, n_out, H, W).  'mlp':
+    head_w o + head_b; 'l2': 1 / (1 + sqrt(|o - e_v|^2 + 1e-8)) with e_v the output-token
+    embeddings (out_embed)."""
     o = x[:, p["out_off"] : p["out_off"] + p["c_out"]]
+    if p.get("head", "mlp") == "l2":
+        e = np.asarray(p["out_embed"], F32)
+        d = o[:, None] - e[None, :, :, None, None]
+        return (F32(1) / (F32(1) + np.sqrt((d * d).sum(axis=2) + F32(1e-8)))).astype(F32)
     hw = p["head_w"].reshape(p["head_w"].shape[0], -1).astype(F32)
     return np.einsum("vc,bchw->bvhw", hw, o).astype(F32) + p["head_b"].astype(F32)[None, :, None, None]
 
@@ -111,8 +120,11 @@ def decode(x, p: dict) -> np.ndarray:
 
 
 def confidence(x, p: dict) -> np.ndarray:
-    """Max softmax probability per cell, clamped to [0, 1] (src/nca/model.py:624-629)."""
+    """Max softmax probability per cell ('mlp' head) or best score ('l2'), clamped to [0, 1]
+    (src/nca/model.py:624-629)."""
     s = scores(x, p)
+    if p.get("head", "mlp") == "l2":
+        return np.clip(s.max(axis=1), 0.0, 1.0).astype(F32)
     m = s.max(axis=1, keepdims=True)
     e = np.exp(s - m)
     return np.clip((e / e.sum(axis=1, keepdims=True)).max(axis=1), 0.0, 1.0).astype(F32)
@@ -427,19 +439,27 @@ def rollout_halving(p: dict, inputs, given, k: int, depth: int, *, channels: int
 
 
 def params_from_arrays(d: dict, cfg) -> dict:
-    """Oracle parameter dict from the reference-named arrays of a model config."""
+    """Oracle parameter dict from the reference-named arrays of a model config (a state dict of
+    the reference's NCA: perceive.weight, update.fc1/fc2, and head.* or out_embed, pad_vec)."""
     n_out = len(cfg.output_tokens)
-    return {
+    p = {
         "taps": np.asarray(d["perceive.weight"], F32).reshape(-1, 9),
         "w1": np.asarray(d["update.fc1.weight"], F32).reshape(d["update.fc1.weight"].shape[0], -1),
         "b1": np.asarray(d["update.fc1.bias"], F32),
         "w2": np.asarray(d["update.fc2.weight"], F32).reshape(d["update.fc2.weight"].shape[0], -1),
         "b2": np.asarray(d["update.fc2.bias"], F32),
-        "head_w": np.asarray(d["head.weight"], F32).reshape(n_out, -1),
-        "head_b": np.asarray(d["head.bias"], F32),
         "out_tokens": np.asarray(cfg.output_tokens),
         "in_off": cfg.in_offset,
         "out_off": cfg.out_offset,
         "c_out": cfg.c_out,
-        "embed": np.eye(cfg.vocab_size, cfg.c_in, dtype=F32),
+        "embed": np.asarray(d["embed"], F32) if "embed" in d else np.eye(cfg.vocab_size, cfg.c_in, dtype=F32),
+        "head": cfg.head,
     }
+    if cfg.head == "l2":
+        p["out_embed"] = np.asarray(d["out_embed"], F32).reshape(n_out, -1)
+    else:
+        p["head_w"] = np.asarray(d["head.weight"], F32).reshape(n_out, -1)
+        p["head_b"] = np.asarray(d["head.bias"], F32)
+    if getattr(cfg, "padding", "zero") == "wall":
+        p["pad"] = np.asarray(d["pad_vec"], F32)
+    return p

@@ -166,6 +166,62 @@ def main() -> None:
 
     np.savez_compressed(OUT, **G)
     print(f"wrote {OUT} ({OUT.stat().st_size / 1e3:.0f} kB, {len(G)} arrays)")
+    presets()
+
+
+def presets() -> None:
+    """The reference's trained maze presets (runs/engine/*_opt/seed0/final.pt) stepped by the
+    reference's own model: their weights and buffers, seeded boards, initial states, external
+    masks and the states after 1 and 12 steps, decoded boards and confidences."""
+    import json
+
+    from nca.tasks.maze import generate_hard_maze as ghm  # noqa: E402
+    from nca.tasks.maze import generate_perfect_maze as gpm  # noqa: E402
+    from nca.train import load_model  # noqa: E402
+
+    P: dict[str, np.ndarray] = {}
+    cases = {
+        "maze_ood": lambda r: gpm(19, r)[:2],
+        "maze_hard": lambda r: ghm(30, r, min_path_len=60, extra_openings=0.10)[:2],
+    }
+    for i, (name, gen) in enumerate(cases.items()):
+        m, _ = load_model(REF / "runs" / "engine" / f"{name}_opt" / "seed0" / "final.pt", device="cpu")
+        ck = torch.load(REF / "runs" / "engine" / f"{name}_opt" / "seed0" / "final.pt",
+                        map_location="cpu", weights_only=False)
+        for k, v in ck["model"].items():
+            P[f"{name}__w__{k}"] = v.float().numpy()
+        P[f"{name}__config"] = np.array(json.dumps(ck["model_config"]))
+        r = np.random.default_rng(51 + i)
+        pairs = [gen(r) for _ in range(3)]
+        inputs = np.stack([a for a, _ in pairs]).astype(np.int64)
+        P[f"{name}__targets"] = np.stack([b for _, b in pairs]).astype(np.uint8)
+        given = inputs != 0
+        inp = torch.from_numpy(inputs)
+        gv = torch.from_numpy(given)
+        with torch.no_grad():
+            x, g4, clamp = m.init_state(inp, gv, None, torch.Generator().manual_seed(3))
+            B, _, H, W = x.shape
+            masks = (np.random.default_rng(61 + i).random((100, B, H * W)) < 0.8).astype(np.uint8)
+            P[f"{name}__x0"] = x.numpy().copy()
+            for t in range(100):
+                fm = torch.from_numpy(masks[t].reshape(B, 1, H, W).astype(np.float32))
+                x = m.step(x, g4, clamp, fm)
+                if t == 0:
+                    P[f"{name}__x1"] = x.numpy().copy()
+                if t == 11:
+                    P[f"{name}__x12"] = x.numpy().copy()
+                    P[f"{name}__dec12"] = torch.where(gv, inp, m.decode(x)).numpy().astype(np.uint8)
+                    P[f"{name}__cconf12"] = m.confidence(x).numpy()
+                    P[f"{name}__bconf12"] = m.board_confidence(x).numpy()
+            # a 100-step rollout (the presets' evaluation depth for maze_ood): decoded boards
+            P[f"{name}__dec100"] = torch.where(gv, inp, m.decode(x)).numpy().astype(np.uint8)
+            P[f"{name}__bconf100"] = m.board_confidence(x).numpy()
+        P[f"{name}__inputs"] = inputs.astype(np.uint8)
+        P[f"{name}__given"] = given
+        P[f"{name}__masks"] = masks
+    out = OUT.parent / "presets.npz"
+    np.savez_compressed(out, **P)
+    print(f"wrote {out} ({out.stat().st_size / 1e3:.0f} kB, {len(P)} arrays)")
 
 
 if __name__ == "__main__":

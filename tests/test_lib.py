@@ -92,7 +92,8 @@ def test_invalid_arguments_are_rejected_without_a_gpu(lib):
 def test_unsupported_cell_rules_raise_value_error():
     check_supported(model_config("maze"))
     check_supported(model_config("sudoku"))
-    for field, value in [("padding", "wall"), ("norm_groups", 4), ("head", "l2"), ("perception", "sobel")]:
+    for field, value in [("padding", "wrap"), ("norm_groups", 4), ("head", "cosine"),
+                         ("perception", "sobel"), ("embedding", "orthonormal"), ("channels", 128)]:
         cfg = model_config("maze")
         setattr(cfg, field, value)
         with pytest.raises(ValueError):

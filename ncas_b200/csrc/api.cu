@@ -57,6 +57,31 @@ __device__ __forceinline__ float clamp_value(const NcaBatchDesc& b, int c_in, in
   return v;
 }
 
+// Copies 16-byte unit u of the state of cell gs to cell gd: hi and lo bf16 units (C/8 units) in
+// the hi/lo layout, else fp32 master units (C/4) and, for even u, the bf16 mirror's unit u/2.
+__device__ __forceinline__ void copy_cell_unit(const float* smaster, const uint16_t* smirror,
+                                               float* dmaster, uint16_t* dmirror, int C, long long gs,
+                                               long long gd, int u) {
+  if (smirror && hilo_layout(C, true)) {
+    const int C8 = C / 8;
+    const long long os = (((gs >> 7) * C8 + u) << 7) + (gs & 127);
+    const long long od = (((gd >> 7) * C8 + u) << 7) + (gd & 127);
+    reinterpret_cast<uint4*>(dmirror)[od] = reinterpret_cast<const uint4*>(smirror)[os];
+    reinterpret_cast<uint4*>(dmaster)[od] = reinterpret_cast<const uint4*>(smaster)[os];
+    return;
+  }
+  const int C4 = C / 4;
+  const long long os = (((gs >> 7) * C4 + u) << 7) + (gs & 127);
+  const long long od = (((gd >> 7) * C4 + u) << 7) + (gd & 127);
+  reinterpret_cast<float4*>(dmaster)[od] = reinterpret_cast<const float4*>(smaster)[os];
+  if (smirror && (u & 1) == 0) {
+    const int C8 = C / 8;
+    const long long ms = (((gs >> 7) * C8 + (u >> 1)) << 7) + (gs & 127);
+    const long long md = (((gd >> 7) * C8 + (u >> 1)) << 7) + (gd & 127);
+    reinterpret_cast<uint4*>(dmirror)[md] = reinterpret_cast<const uint4*>(smirror)[ms];
+  }
+}
+
 // The clamp of src/nca/model.py:430-438 on the current state: one thread per cell writes the
 // clamp values over the input slice of the given cells (fp32 state and bf16 mirror).  Run after
 // the first step on a state that was not clamped (loaded from outside the library); the step
@@ -69,15 +94,8 @@ __global__ void clamp_fix_kernel(float* master, uint16_t* mirror, int C, long lo
   const int p = (int)(g - (long long)inst * hw);
   const int row = b.inst_row ? b.inst_row[inst] : inst / b.trials;
   if (!b.given[(long long)row * hw + p]) return;
-  const long long t = g >> 7;
-  const int m = (int)(g & 127);
-  for (int ci = 0; ci < c_in; ++ci) {
-    const int c = in_off + ci;
-    const float v = b.clamp[((long long)row * hw + p) * c_in + ci];
-    master[((t * (C / 4) + (c >> 2)) * kTileM + m) * 4 + (c & 3)] = v;
-    if (mirror)
-      mirror[((t * (C / 8) + (c >> 3)) * kTileM + m) * 8 + (c & 7)] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
-  }
+  for (int ci = 0; ci < c_in; ++ci)
+    state_put(master, mirror, C, g, in_off + ci, b.clamp[((long long)row * hw + p) * c_in + ci]);
 }
 
 // Damage (src/nca/rollout.py:206-212): one thread per cell; a masked cell gets a zero state, and
@@ -90,15 +108,11 @@ __global__ void damage_kernel(float* master, uint16_t* mirror, int C, long long 
   const int p = (int)(g - (long long)inst * hw);
   const int row = b.inst_row ? b.inst_row[inst] : inst / b.trials;
   if (!masks[(long long)row * hw + p]) return;
-  const long long t = g >> 7;
-  const int m = (int)(g & 127);
   const bool gv = b.given[(long long)row * hw + p] != 0;
   for (int c = 0; c < C; ++c) {
     const int ci = c - in_off;
     const float v = (gv && ci >= 0 && ci < c_in) ? b.clamp[((long long)row * hw + p) * c_in + ci] : 0.f;
-    master[((t * (C / 4) + (c >> 2)) * kTileM + m) * 4 + (c & 3)] = v;
-    if (mirror)
-      mirror[((t * (C / 8) + (c >> 3)) * kTileM + m) * 8 + (c & 7)] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+    state_put(master, mirror, C, g, c, v);
   }
 }
 
@@ -128,23 +142,31 @@ __global__ void state_fill_kernel(float* master, uint16_t* mirror, int C, long l
       v[e] = x;
     }
   }
-  for (int hq = 0; hq < 2; ++hq) {
-    const int c4 = c8 * 2 + hq;
-    *reinterpret_cast<float4*>(master + ((t * (C / 4) + c4) * kTileM + m) * 4) =
-        make_float4(v[hq * 4 + 0], v[hq * 4 + 1], v[hq * 4 + 2], v[hq * 4 + 3]);
-  }
-  if (mirror) {
-    uint4 pk;
-    pk.x = pack_bf16(v[0], v[1]);
-    pk.y = pack_bf16(v[2], v[3]);
-    pk.z = pack_bf16(v[4], v[5]);
-    pk.w = pack_bf16(v[6], v[7]);
-    *reinterpret_cast<uint4*>(mirror + ((t * (C / 8) + c8) * kTileM + m) * 8) = pk;
+  if (mirror && hilo_layout(C, true)) {  // hi and lo parts
+    uint32_t h[4], l[4];
+    for (int e = 0; e < 4; ++e) {
+      h[e] = pack_bf16(v[2 * e], v[2 * e + 1]);
+      l[e] = pack_bf16(v[2 * e] - bf16lo_to_f32(h[e]), v[2 * e + 1] - bf16hi_to_f32(h[e]));
+    }
+    const long long o = ((t * (C / 8) + c8) * kTileM + m) * 8;
+    *reinterpret_cast<uint4*>(mirror + o) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(master) + o) = make_uint4(l[0], l[1], l[2], l[3]);
+  } else {
+    for (int hq = 0; hq < 2; ++hq) {
+      const int c4 = c8 * 2 + hq;
+      *reinterpret_cast<float4*>(master + ((t * (C / 4) + c4) * kTileM + m) * 4) =
+          make_float4(v[hq * 4 + 0], v[hq * 4 + 1], v[hq * 4 + 2], v[hq * 4 + 3]);
+    }
+    if (mirror) {
+      const uint4 pk = make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]),
+                                  pack_bf16(v[6], v[7]));
+      *reinterpret_cast<uint4*>(mirror + ((t * (C / 8) + c8) * kTileM + m) * 8) = pk;
+    }
   }
 }
 
-__global__ void state_store_kernel(const float* master, int C, long long total, int hw,
-                                   float* x_nchw) {
+__global__ void state_store_kernel(const float* master, const uint16_t* mirror, int C,
+                                   long long total, int hw, float* x_nchw) {
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= total * C) return;
   // idx enumerates NCHW order: ((inst * C + c) * hw + p)
@@ -152,10 +174,7 @@ __global__ void state_store_kernel(const float* master, int C, long long total, 
   const long long r = idx / hw;
   const int c = (int)(r % C);
   const long long inst = r / C;
-  const long long g = inst * hw + p;
-  const long long t = g >> 7;
-  const int m = (int)(g & 127);
-  x_nchw[idx] = master[((t * (C / 4) + (c >> 2)) * kTileM + m) * 4 + (c & 3)];
+  x_nchw[idx] = state_get(master, mirror, C, inst * hw + p, c);
 }
 
 // ------------------------------------------------------------------------------- readout
@@ -169,7 +188,7 @@ struct ReadoutArgs {
 // One block per instance.  head_readout of every cell (argmax as torch.argmax, the head's
 // confidence clamped to [0, 1], src/nca/model.py:596-633), the decoded token (given cells show
 // their input, src/nca/rollout.py:74-82), the board confidence and, with targets, the accuracy.
-__global__ void readout_kernel(const float* master, NcaBatchDesc b, ReadoutArgs R, uint8_t* pred,
+__global__ void readout_kernel(const float* master, const uint16_t* mirror, NcaBatchDesc b, ReadoutArgs R, uint8_t* pred,
                                float* cell_conf, float* board_conf, const uint8_t* targets,
                                float* cell_acc, uint8_t* exact) {
   const int inst = blockIdx.x;
@@ -177,16 +196,11 @@ __global__ void readout_kernel(const float* master, NcaBatchDesc b, ReadoutArgs 
   float conf_sum = 0.f, correct = 0.f, n_mut = 0.f;
   for (int p = threadIdx.x; p < R.hw; p += blockDim.x) {
     const long long g = (long long)inst * R.hw + p;
-    const long long t = g >> 7;
-    const int m = (int)(g & 127);
     float xo[16];
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
       xo[c] = 0.f;
-      if (c < R.c_out) {
-        const int cc = R.out_off + c;
-        xo[c] = master[((t * (R.C / 4) + (cc >> 2)) * kTileM + m) * 4 + (cc & 3)];
-      }
+      if (c < R.c_out) xo[c] = state_get(master, mirror, R.C, g, R.out_off + c);
     }
     float conf;
     int arg;
@@ -415,50 +429,32 @@ __global__ void halving_kernel(const int* niche, const int* rank, const int* n_n
   }
 }
 
-// One thread per (destination instance, cell, 4-channel chunk): dst instance i <- src sel[i].
+// One thread per (destination instance, cell, 16-byte unit): dst instance i <- src sel[i].
 __global__ void gather_kernel(const float* smaster, const uint16_t* smirror, float* dmaster,
                               uint16_t* dmirror, int C, int hw, int n_dst, const int* sel) {
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const int C4 = C / 4;
-  if (idx >= (long long)n_dst * hw * C4) return;
-  const int c4 = (int)(idx % C4);
-  const long long g = idx / C4;
+  const int U = (smirror && hilo_layout(C, true)) ? C / 8 : C / 4;
+  if (idx >= (long long)n_dst * hw * U) return;
+  const int u = (int)(idx % U);
+  const long long g = idx / U;
   const int i = (int)(g / hw);
   const int p = (int)(g - (long long)i * hw);
-  const long long gs = (long long)sel[i] * hw + p;
-  const float4* src = reinterpret_cast<const float4*>(smaster) + ((gs >> 7) * C4 + c4) * kTileM + (gs & 127);
-  float4* dst = reinterpret_cast<float4*>(dmaster) + ((g >> 7) * C4 + c4) * kTileM + (g & 127);
-  *dst = *src;
-  if (smirror && (c4 & 1) == 0) {
-    const int c8 = c4 >> 1, C8 = C / 8;
-    const uint4* ms = reinterpret_cast<const uint4*>(smirror) + ((gs >> 7) * C8 + c8) * kTileM + (gs & 127);
-    uint4* md = reinterpret_cast<uint4*>(dmirror) + ((g >> 7) * C8 + c8) * kTileM + (g & 127);
-    *md = *ms;
-  }
+  copy_cell_unit(smaster, smirror, dmaster, dmirror, C, (long long)sel[i] * hw + p, g, u);
 }
 
-// One thread per (instance, cell, 4-channel chunk) of the destination.
+// One thread per (destination instance, cell, 16-byte unit of the state).
 __global__ void clone_kernel(float* master, uint16_t* mirror, int C, int hw, int n_inst,
                              const int* src) {
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const int C4 = C / 4;
-  if (idx >= (long long)n_inst * hw * C4) return;
-  const int c4 = (int)(idx % C4);
-  const long long cell = idx / C4;
+  const int U = (mirror && hilo_layout(C, true)) ? C / 8 : C / 4;
+  if (idx >= (long long)n_inst * hw * U) return;
+  const int u = (int)(idx % U);
+  const long long cell = idx / U;
   const int inst = (int)(cell / hw);
   const int p = (int)(cell - (long long)inst * hw);
   const int s = src[inst];
   if (s == inst) return;
-  const long long gd = (long long)inst * hw + p, gs = (long long)s * hw + p;
-  const long long od = (((gd >> 7) * C4 + c4) << 7) + (gd & 127);
-  const long long os = (((gs >> 7) * C4 + c4) << 7) + (gs & 127);
-  reinterpret_cast<float4*>(master)[od] = reinterpret_cast<const float4*>(master)[os];
-  if (mirror && (c4 & 1) == 0) {
-    const int C8 = C / 8, c8 = c4 >> 1;
-    const long long md = (((gd >> 7) * C8 + c8) << 7) + (gd & 127);
-    const long long ms = (((gs >> 7) * C8 + c8) << 7) + (gs & 127);
-    reinterpret_cast<uint4*>(mirror)[md] = reinterpret_cast<const uint4*>(mirror)[ms];
-  }
+  copy_cell_unit(master, mirror, master, mirror, C, (long long)s * hw + p, (long long)inst * hw + p, u);
 }
 
 __global__ void selftest_wait_kernel(int* ctrl, unsigned long long timeout_ns) {
@@ -545,10 +541,12 @@ int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaState* st,
   A.ctrl = ctrl;
   A.timeout_ns = (unsigned long long)(timeout_ms > 0 ? timeout_ms : 10000) * 1000000ull;
 
-  int stages = 2;
+  // Window stages: in the hi/lo layout a window lives from the stencil to the epilogue (which
+  // reads the hi part of the old state from it), so more stages keep the stencil ahead.
+  int stages = Cfg::HILO ? kMaxStages : 2;
   int smem = SmemLayout<Cfg>(stages, A.win_cells, A.wimg_lo != nullptr).total + 1024;
-  if (smem > kMaxSmem) {
-    stages = 1;
+  while (smem > kMaxSmem && stages > 1) {
+    --stages;
     smem = SmemLayout<Cfg>(stages, A.win_cells, A.wimg_lo != nullptr).total + 1024;
   }
   if (smem > kMaxSmem) return NCA_ERR_UNSUPPORTED;
@@ -660,7 +658,9 @@ int32_t nca_b200_state_bytes(int32_t n_inst, int32_t hw, int32_t channels, int32
                              size_t* bytes) {
   if (!bytes || n_inst <= 0 || hw <= 0 || channels <= 0 || channels % 16) return NCA_ERR_INVALID;
   const long long tiles = n_tiles_of((long long)n_inst * hw);
-  const size_t master = align256((size_t)tiles * kTileM * channels * 4);
+  // fp32 master (+ bf16 mirror in bf16 mode), or hi (mirror) and lo (master) bf16 arrays
+  const bool hl = hilo_layout(channels, precision == NCA_PREC_BF16);
+  const size_t master = align256((size_t)tiles * kTileM * channels * (hl ? 2 : 4));
   const size_t mirror = precision == NCA_PREC_BF16 ? align256((size_t)tiles * kTileM * channels * 2) : 0;
   *bytes = 2 * master + 2 * mirror;
   return NCA_OK;
@@ -675,7 +675,8 @@ int32_t nca_b200_state_bind(NcaState* st, void* buffer, size_t bytes, int32_t n_
     return NCA_ERR_INVALID;
   if (precision != NCA_PREC_BF16 && precision != NCA_PREC_SPLIT) return NCA_ERR_INVALID;
   const long long tiles = n_tiles_of((long long)n_inst * hw);
-  const size_t master = align256((size_t)tiles * kTileM * channels * 4);
+  const bool hl = hilo_layout(channels, precision == NCA_PREC_BF16);
+  const size_t master = align256((size_t)tiles * kTileM * channels * (hl ? 2 : 4));
   const size_t mirror = precision == NCA_PREC_BF16 ? align256((size_t)tiles * kTileM * channels * 2) : 0;
   uint8_t* p = reinterpret_cast<uint8_t*>(buffer);
   st->n_inst = n_inst;
@@ -724,7 +725,8 @@ int32_t nca_b200_state_store_nchw(const NcaState* st, float* x_nchw, void* strea
   const long long n = (long long)st->n_inst * st->hw * st->channels;
   const int bs = 256;
   state_store_kernel<<<(unsigned)((n + bs - 1) / bs), bs, 0, as_stream(stream)>>>(
-      st->master[st->cur], st->channels, (long long)st->n_inst * st->hw, st->hw, x_nchw);
+      st->master[st->cur], st->mirror[st->cur], st->channels, (long long)st->n_inst * st->hw, st->hw,
+      x_nchw);
   return cuda_status(cudaGetLastError());
 }
 
@@ -801,7 +803,7 @@ int32_t nca_b200_readout(const NcaModelDesc* m, const NcaBatchDesc* b, const Nca
   memcpy(R.head_w, m->head_w, sizeof(R.head_w));
   memcpy(R.head_b, m->head_b, sizeof(R.head_b));
   memcpy(R.out_tokens, m->out_tokens, sizeof(R.out_tokens));
-  readout_kernel<<<st->n_inst, 128, 0, as_stream(stream)>>>(st->master[st->cur], *b, R, pred,
+  readout_kernel<<<st->n_inst, 128, 0, as_stream(stream)>>>(st->master[st->cur], st->mirror[st->cur], *b, R, pred,
                                                            cell_conf, board_conf, targets,
                                                            cell_acc, exact);
   return cuda_status(cudaGetLastError());
@@ -835,7 +837,8 @@ int32_t nca_b200_prune_refill(const uint8_t* pred, const float* board_conf, int3
 
 int32_t nca_b200_clone(NcaState* st, const int32_t* src, void* stream) {
   if (!st || !src) return NCA_ERR_INVALID;
-  const long long n = (long long)st->n_inst * st->hw * (st->channels / 4);
+  const bool hl = st->mirror[0] && hilo_layout(st->channels, true);
+  const long long n = (long long)st->n_inst * st->hw * (st->channels / (hl ? 8 : 4));
   const int bs = 256;
   clone_kernel<<<(unsigned)((n + bs - 1) / bs), bs, 0, as_stream(stream)>>>(
       st->master[st->cur], st->mirror[st->cur], st->channels, st->hw, st->n_inst, src);
@@ -888,7 +891,8 @@ int32_t nca_b200_gather(const NcaState* src, NcaState* dst, const int32_t* sel, 
   if (src->channels != dst->channels || src->hw != dst->hw || src->precision != dst->precision ||
       dst->n_inst > src->n_inst)
     return NCA_ERR_INVALID;
-  const long long n = (long long)dst->n_inst * dst->hw * (dst->channels / 4);
+  const bool hl = dst->mirror[0] && hilo_layout(dst->channels, true);
+  const long long n = (long long)dst->n_inst * dst->hw * (dst->channels / (hl ? 8 : 4));
   if (n > 0) {
     const int bs = 256;
     gather_kernel<<<(unsigned)((n + bs - 1) / bs), bs, 0, as_stream(stream)>>>(

@@ -36,6 +36,11 @@ constexpr int pow2ceil(int v) {
   return p;
 }
 
+// State layout of a model (see state_get): bf16 mode keeps hi + lo bf16 parts when C >= 64 (the
+// MMA work per cell hides the extra packing, and a step moves 512 instead of 768 bytes per
+// cell), else an fp32 master plus a bf16 mirror for the stencil; split mode keeps fp32.
+__host__ __device__ constexpr bool hilo_layout(int C, bool bf16) { return bf16 && C >= 64; }
+
 template <int C_, int HD_, bool SPLIT_, bool NOISE_ = false>
 struct StepCfg {
   static constexpr int C = C_;
@@ -44,6 +49,7 @@ struct StepCfg {
   static constexpr int HD = HD_;
   static constexpr bool SPLIT = SPLIT_;
   static constexpr bool SRC_BF16 = !SPLIT_;
+  static constexpr bool HILO = hilo_layout(C_, !SPLIT_);
   static constexpr int SRC_BYTES = SRC_BF16 ? 2 : 4;
   static constexpr int ROWB = C * SRC_BYTES;         // bytes of one cell in a window stage
   static constexpr int NCH = ROWB / 16;              // 16-byte chunks per cell
@@ -138,25 +144,27 @@ struct SmemLayout {
     b2 = b1 + Cfg::HD * 4;
     flags = b2 + Cfg::C * 4;
     bars = (flags + 4 * kTileM + 7) & ~7;
-    misc = bars + 24 * 8;
+    misc = bars + 24 * 8;  // BAR_COUNT <= 24 barriers
     total = misc + 64;
   }
 };
 
+constexpr int kMaxStages = 4;  // window stages
 enum BarId {
-  BAR_WIN_FULL = 0,   // +stage (2)
-  BAR_WIN_EMPTY = 2,  // +stage (2)
-  BAR_Z_FULL = 4,     // +slot (2)
-  BAR_Z_EMPTY = 6,    // +slot (2)
-  BAR_ACC_FULL = 8,
-  BAR_H_FULL = 9,
-  BAR_ACC2_FULL = 10,
-  BAR_ACC_EMPTY = 11,
-  BAR_WEIGHTS = 12,
-  BAR_DRAIN = 13,
-  BAR_ACC_FULL_B = 14,  // second half of GEMM1 (hidden units HD/2 .. HD)
-  BAR_H_FULL_B = 15,    // second half of the hidden epilogue
-  BAR_FLAGS = 16,       // +ring index (4): per-row fire/given flags of a tile are written
+  BAR_WIN_FULL = 0,   // +stage (4)
+  BAR_WIN_EMPTY = 4,  // +stage (4)
+  BAR_Z_FULL = 8,     // +slot (2)
+  BAR_Z_EMPTY = 10,   // +slot (2)
+  BAR_ACC_FULL = 12,
+  BAR_H_FULL = 13,
+  BAR_ACC2_FULL = 14,
+  BAR_ACC_EMPTY = 15,
+  BAR_WEIGHTS = 16,
+  BAR_DRAIN = 17,
+  BAR_ACC_FULL_B = 18,  // second half of GEMM1 (hidden units HD/2 .. HD)
+  BAR_H_FULL_B = 19,    // second half of the hidden epilogue
+  BAR_FLAGS = 20,       // +ring index (4): per-row fire/given flags of a tile are written
+  BAR_COUNT = 24
 };
 
 // Failure sites reported in ctrl[1].
@@ -230,6 +238,39 @@ __device__ __forceinline__ void fixed_taps4(float a, float b, float c, float d, 
   lap = s * 0.0625f;
 }
 
+// The state of a cell channel.  fp32 layout: master [tile][C/4][128][4] (split mode, and bf16
+// mode below 64 channels, with a bf16 copy [tile][C/8][128][8] in `mirror` for the stencil).
+// hi/lo layout (bf16 mode, C >= 64): two bf16 values [tile][C/8][128][8], hi = bf16(x) in
+// `mirror` (the array the stencil reads) and lo = bf16(x - hi) in `master` (reinterpreted), so
+// x = hi + lo carries about 16 significant bits and a step reads and writes 4 bytes per channel.
+__host__ __device__ __forceinline__ long long sidx8(long long g, int C, int c) {
+  return (((g >> 7) * (C / 8) + (c >> 3)) * 128 + (g & 127)) * 8 + (c & 7);
+}
+__host__ __device__ __forceinline__ long long sidx4(long long g, int C, int c) {
+  return (((g >> 7) * (C / 4) + (c >> 2)) * 128 + (g & 127)) * 4 + (c & 3);
+}
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
+__device__ __forceinline__ float state_get(const float* master, const uint16_t* mirror, int C,
+                                           long long g, int c) {
+  if (mirror && hilo_layout(C, true)) {
+    const long long i = sidx8(g, C, c);
+    return bf16_bits_to_f32(mirror[i]) + bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(master)[i]);
+  }
+  return master[sidx4(g, C, c)];
+}
+__device__ __forceinline__ void state_put(float* master, uint16_t* mirror, int C, long long g, int c,
+                                          float v) {
+  if (mirror && hilo_layout(C, true)) {
+    const long long i = sidx8(g, C, c);
+    const uint16_t h = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+    mirror[i] = h;
+    reinterpret_cast<uint16_t*>(master)[i] = __bfloat16_as_ushort(__float2bfloat16_rn(v - bf16_bits_to_f32(h)));
+  } else {
+    master[sidx4(g, C, c)] = v;
+    if (mirror) mirror[sidx8(g, C, c)] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  }
+}
+
 // Readout of one cell from its readout slice xs[0 .. c_out) (src/nca/model.py:596-633):
 // kind 0 (head "mlp"): scores head_w x + head_b, confidence the max softmax;
 // kind 1 (head "l2"): rows of head_w are the output-token embeddings e_o, score
@@ -283,17 +324,24 @@ __device__ __forceinline__ void head_readout(int kind, int n_out, int c_out, con
 // threshold rule (src/nca/model.py:566-593) p = p_low for confident cells (conf > tau, or given
 // cells when given_confident), else p_fire; fire when u < p with u from Philox or the caller.
 // Read from the fp32 state of the step's input buffer (complete since the last grid barrier).
+// xhi: in the hi/lo layout, the hi parts of the readout slice (read from the window stage by
+// the caller while the stage is still its own); the lo parts come from global memory.
 template <class Cfg>
 __device__ __forceinline__ bool adaptive_fire(const StepArgs& A, int s, long long t, int m, int inst,
-                                              int p, bool given) {
+                                              int p, bool given, const float (&xhi)[16]) {
   const float* xin = A.master[(A.cur + s) & 1];
+  const long long g = t * kTileM + m;
   float xs[16];
 #pragma unroll
   for (int c = 0; c < 16; ++c) {
     xs[c] = 0.f;
     if (c < A.c_out) {
       const int cc = A.out_off + c;
-      xs[c] = __ldg(xin + ((((t * (Cfg::C / 4) + (cc >> 2)) << 7) + m) * 4 + (cc & 3)));
+      if constexpr (Cfg::HILO) {
+        xs[c] = xhi[c] + bf16_bits_to_f32(__ldg(reinterpret_cast<const unsigned short*>(xin) + sidx8(g, Cfg::C, cc)));
+      } else {
+        xs[c] = __ldg(xin + sidx4(g, Cfg::C, cc));
+      }
     }
   }
   float conf;
@@ -334,9 +382,13 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kMaxStages; ++s) {
       mbar_init(&bars[BAR_WIN_FULL + s], 1);
+      // released by the 8 stencil warps, or in bf16 mode by the 8 epilogue warps, which read
+      // the hi part of the old state from the window
       mbar_init(&bars[BAR_WIN_EMPTY + s], 8);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&bars[BAR_Z_FULL + s], 8);
       mbar_init(&bars[BAR_Z_EMPTY + s], 1);
     }
@@ -729,12 +781,30 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
             }
           }
         }
+        // adaptive rules in the hi/lo layout: the hi parts of the readout slice are read from the
+        // window now, before z is handed off (the epilogue releases the stage after that)
+        float xhi[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) xhi[c] = 0.f;
+        if constexpr (Cfg::HILO) {
+          if (half == 0 && A.fire_mode >= 2 && valid) {
+#pragma unroll
+            for (int c = 0; c < 16; ++c)
+              if (c < A.c_out) {
+                const int cc = A.out_off + c;
+                xhi[c] = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(
+                    win + ((cc >> 3) * (WC + 1) + c0) * 16 + (cc & 7) * 2));
+              }
+          }
+        }
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
           mbar_arrive_relaxed(&bars[BAR_Z_FULL + slot]);
-          mbar_arrive_relaxed(&bars[BAR_WIN_EMPTY + stage]);
+          // hi/lo layout: the epilogue still reads the tile's own cells (the hi part of the old
+          // state) from this window and releases it
+          if constexpr (!Cfg::HILO) mbar_arrive_relaxed(&bars[BAR_WIN_EMPTY + stage]);
         }
         if (half == 0 && A.fire_mode >= 2) {
           // adaptive rules: the fire decision needs the confidence of the cell's fp32 state; it
@@ -744,7 +814,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
             const int row = A.inst_row ? A.inst_row[inst] : (int)fdiv((unsigned)inst, A.div_k);
             const bool gv = A.given[(long long)row * A.HW + p] != 0;
             fl = 4u | (gv ? 2u : 0u);
-            fl |= adaptive_fire<Cfg>(A, s, t, m, inst, p, gv) ? 1u : 0u;
+            fl |= adaptive_fire<Cfg>(A, s, t, m, inst, p, gv, xhi) ? 1u : 0u;
           }
           s_flags[(it & 3) * kTileM + m] = (uint8_t)fl;
           __syncwarp();
@@ -822,9 +892,31 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         // ---- E2: dx = acc2 + b2; x' = x + f * dx; clamp; store.  The old state of this thread's
         // channels is loaded while GEMM2 runs.
         float4 xo[NQ];
+        if constexpr (Cfg::HILO) {
+          // old state = hi, this tile's own cells in the window stage of the stencil, + lo from
+          // global memory
+          const uint4* lo4 = reinterpret_cast<const uint4*>(xin) + ((t * (Cfg::C / 8) + half * (CH / 8)) << 7) + m;
+          const uint8_t* wst = smem + L.win + (int)(it % A.stages) * (A.win_cells + 1) * Cfg::ROWB;
 #pragma unroll
-        for (int q = 0; q < NQ; ++q) xo[q] = valid ? __ldg(xin4 + (q << 7)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int j = 0; j < CH / 8; ++j) {
+            const uint4 lo = valid ? __ldg(lo4 + (j << 7)) : make_uint4(0u, 0u, 0u, 0u);
+            const uint4 hi = *reinterpret_cast<const uint4*>(
+                wst + ((half * (CH / 8) + j) * (A.win_cells + 1) + (m + W + 1)) * 16);
+            xo[2 * j] = make_float4(bf16lo_to_f32(hi.x) + bf16lo_to_f32(lo.x), bf16hi_to_f32(hi.x) + bf16hi_to_f32(lo.x),
+                                    bf16lo_to_f32(hi.y) + bf16lo_to_f32(lo.y), bf16hi_to_f32(hi.y) + bf16hi_to_f32(lo.y));
+            xo[2 * j + 1] = make_float4(bf16lo_to_f32(hi.z) + bf16lo_to_f32(lo.z), bf16hi_to_f32(hi.z) + bf16hi_to_f32(lo.z),
+                                        bf16lo_to_f32(hi.w) + bf16lo_to_f32(lo.w), bf16hi_to_f32(hi.w) + bf16hi_to_f32(lo.w));
+          }
+          // the stencil warps finished every read of this window before handing z to the MMA
+          // warp, and this warp has its hi values: release the stage to the loader
+          __syncwarp();
+          if (lane == 0) mbar_arrive_relaxed(&bars[BAR_WIN_EMPTY + (int)(it % A.stages)]);
+        } else {
+#pragma unroll
+          for (int q = 0; q < NQ; ++q) xo[q] = valid ? __ldg(xin4 + (q << 7)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
         if (!warp_wait(&bars[BAR_FLAGS + (it & 3)], (uint32_t)(it >> 2) & 1, fs, W_E2_FLAGS)) { ok = false; break; }
+
         const uint32_t fl = s_flags[(it & 3) * kTileM + m];
         const bool gv = (fl & 2u) != 0;
         const float f = (fl & 1u) ? 1.f : 0.f;
@@ -860,7 +952,8 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           // the bf16 mirror of each 8 channels is stored as soon as they are done (fewer live
           // registers than packing all of them first)
           uint4* mout4 = reinterpret_cast<uint4*>(mout) + ((t * (Cfg::C / 8) + half * (CH / 8)) << 7) + m;
-          uint32_t pk[4];
+          uint4* lout4 = reinterpret_cast<uint4*>(xout) + ((t * (Cfg::C / 8) + half * (CH / 8)) << 7) + m;
+          uint32_t pk[4], pl[4];
           // Test-time noise (src/nca/perturb.py:23-40): added after the update, before the clamp
           // (src/nca/model.py:544-546); only the NOISE instantiation carries this code.
           bool nz = false;
@@ -908,11 +1001,24 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
             y0.y = (keep >> (4 * q + 1)) & 1u ? xo[q].y : y0.y;
             y1.x = (keep >> (4 * q + 2)) & 1u ? xo[q].z : y1.x;
             y1.y = (keep >> (4 * q + 3)) & 1u ? xo[q].w : y1.y;
-            xout4[q << 7] = make_float4(y0.x, y0.y, y1.x, y1.y);
-            if constexpr (Cfg::SRC_BF16) {
-              pk[2 * (q & 1)] = pack_bf16(y0.x, y0.y);
-              pk[2 * (q & 1) + 1] = pack_bf16(y1.x, y1.y);
-              if (q & 1) mout4[(q >> 1) << 7] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            if constexpr (Cfg::HILO) {
+              // hi = bf16(y) to the mirror, lo = bf16(y - hi) to the low array
+              const uint32_t h0 = pack_bf16(y0.x, y0.y), h1 = pack_bf16(y1.x, y1.y);
+              pk[2 * (q & 1)] = h0;
+              pk[2 * (q & 1) + 1] = h1;
+              pl[2 * (q & 1)] = pack_bf16(y0.x - bf16lo_to_f32(h0), y0.y - bf16hi_to_f32(h0));
+              pl[2 * (q & 1) + 1] = pack_bf16(y1.x - bf16lo_to_f32(h1), y1.y - bf16hi_to_f32(h1));
+              if (q & 1) {
+                mout4[(q >> 1) << 7] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                lout4[(q >> 1) << 7] = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+              }
+            } else {
+              xout4[q << 7] = make_float4(y0.x, y0.y, y1.x, y1.y);
+              if constexpr (Cfg::SRC_BF16) {  // the stencil's bf16 copy
+                pk[2 * (q & 1)] = pack_bf16(y0.x, y0.y);
+                pk[2 * (q & 1) + 1] = pack_bf16(y1.x, y1.y);
+                if (q & 1) mout4[(q >> 1) << 7] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              }
             }
           }
         }

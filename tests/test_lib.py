@@ -73,9 +73,9 @@ def test_state_bytes(lib):
     n = C.c_size_t(0)
     assert lib.nca_b200_state_bytes(1000, 81, 64, L.PREC_BF16, C.byref(n)) == 0
     tiles = -(-1000 * 81 // 128)
-    master = tiles * 128 * 64 * 4
-    mirror = tiles * 128 * 64 * 2
-    assert n.value == 2 * master + 2 * mirror
+    lo = tiles * 128 * 64 * 2  # bf16 mode: hi (mirror) and lo bf16 arrays, two buffers each
+    hi = tiles * 128 * 64 * 2
+    assert n.value == 2 * lo + 2 * hi
     assert lib.nca_b200_state_bytes(10, 81, 64, L.PREC_SPLIT, C.byref(n)) == 0
     assert n.value == 2 * (-(-810 // 128) * 128 * 64 * 4 + 255 & ~255)
     assert lib.nca_b200_state_bytes(0, 81, 64, 0, C.byref(n)) == 1

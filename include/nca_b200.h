@@ -270,7 +270,7 @@ int32_t nca_b200_selftest_timeout(int32_t* ctrl, int32_t timeout_ms, void* strea
  * the caller allocates; the caller passes only inputs and outputs: the fp32 NCHW state before
  * (x_in) and after (x_out) the steps, both n_inst x channels x H x W.
  *  - Limit: nca_b200_state_bytes(n_inst, H*W, channels, state_precision) + 256 bytes must fit in
- *    NCA_B200_STATIC_SCRATCH_BYTES, else NCA_ERR_SCRATCH (e.g. 21,000 Sudoku cells at C = 64 or one
+ *    NCA_B200_STATIC_SCRATCH_BYTES, else NCA_ERR_SCRATCH (e.g. 32,000 Sudoku cells at C = 64 or one
  *    201 x 201 maze at C = 32 in bf16 mode).
  *  - It calls no allocator.  Its first call on a device looks up the device address of the array
  *    (cudaGetSymbolAddress with that device current); make that first call before any stream

@@ -3,16 +3,19 @@
 // One CTA per SM.  Each step, every instance's cells are processed in tiles of 128 consecutive
 // cells (global cell index g = inst * H * W + i * W + j).  Per tile:
 //
-//   loader warp    cp.async of the tile's halo window (cells g0-W-1 .. g0+128+W) of the
-//                  previous state into a bank-swizzled shared-memory stage
-//   stencil warps  one thread per tile row: 3x3 perception with zero padding (4 heads, head-major
-//                  z[k*C + c] as nca.model.KernelPerception, src/nca/model.py:175-178), written
-//                  as bf16 (hi, lo) pairs straight into tensor memory: the A operand of GEMM1
+//   loader warp    1-D bulk copies (cp.async.bulk) of the tile's halo window (cells
+//                  g0-W-1 .. g0+128+W) of the previous state into a shared-memory stage laid out
+//                  [chunk][cell][16 B], each chunk row ending in a padding cell
+//   stencil warps  one thread per tile row and half of the channels: 3x3 perception (4 heads,
+//                  head-major z[k*C + c] as nca.model.KernelPerception, src/nca/model.py:
+//                  175-178; neighbours outside the board read the padding cell) written as bf16
+//                  (bf16 hi + lo in split mode) into tensor memory, the A operand of GEMM1; the
+//                  half-0 warps also write the per-row fire / given flags of the step
 //   MMA thread     GEMM1 acc1 = z W1^T (tcgen05.mma kind::f16, A from TMEM, B = fc1.weight in
 //                  128B-swizzled smem), then after the hidden epilogue GEMM2 acc2 = h W2^T
 //   epilogue warps E1: h = relu(acc1 + b1) -> bf16 back into TMEM (A operand of GEMM2);
-//                  E2: dx = acc2 + b2, fire mask, x' = x + f*dx, clamp, store (src/nca/model.py:
-//                  527-559, 430-438)
+//                  E2: dx = acc2 + b2, fire mask (+ noise), x' = x + f*dx, clamp, store
+//                  (src/nca/model.py:527-559, 430-438)
 //
 // Tensor memory (512 columns x 128 lanes): NZ slots holding z and one accumulator region
 // holding acc1, then h (bf16, over the columns already read) and acc2.  Every wait is bounded; a

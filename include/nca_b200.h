@@ -118,6 +118,8 @@ typedef struct NcaState {
   int32_t clamped;          /* 1 when the given cells of the current state hold their clamp
                                values (set by nca_b200_state_init and by every step; cleared by
                                nca_b200_state_bind and nca_b200_state_load_nchw) */
+  uint32_t* tile_steps;     /* device [n_tiles]: per-tile step counters of a launch (the step
+                               kernel's dependencies between neighbouring tiles) */
 } NcaState;
 
 typedef enum NcaNoiseMode {

@@ -85,6 +85,7 @@ class NcaState(C.Structure):
         ("mirror", C.c_void_p * 2),
         ("cur", C.c_int32),
         ("clamped", C.c_int32),
+        ("tile_steps", C.c_void_p),
     ]
 
 

@@ -557,11 +557,22 @@ int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaState* st,
   if (e != cudaSuccess) return NCA_ERR_CUDA;
   e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return NCA_ERR_CUDA;
-  auto kern = nca_step_kernel<Cfg>;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return NCA_ERR_CUDA;
   const long long grid_ll = A.n_tiles < sms ? A.n_tiles : sms;
   const int grid = (int)(grid_ll > 0 ? grid_ll : 1);
+  // Steps are ordered by per-tile step counters when every CTA has few tiles (a grid barrier
+  // would idle the whole GPU at each step boundary), else by the grid barrier on ctrl[2], whose
+  // cost is then small against the step (the per-tile form costs the epilogue registers and the
+  // MMA warp a publisher lane).
+  const bool tiledep = n_steps > 1 && A.n_tiles <= (long long)kTileDepPerCta * grid;
+  using CfgTD = StepCfg<Cfg::C, Cfg::HD, Cfg::SPLIT, Cfg::NOISE, true>;
+  auto kern = tiledep ? nca_step_kernel<CfgTD> : nca_step_kernel<Cfg>;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return NCA_ERR_CUDA;
+  A.tile_steps = tiledep ? st->tile_steps : nullptr;
+  if (tiledep) {
+    e = cudaMemsetAsync(st->tile_steps, 0, (size_t)st->n_tiles * sizeof(uint32_t), stream);
+    if (e != cudaSuccess) return NCA_ERR_CUDA;
+  }
   e = cudaMemsetAsync(ctrl + 2, 0, sizeof(int32_t), stream);
   if (e != cudaSuccess) return NCA_ERR_CUDA;
   if (n_steps > 1) {
@@ -662,7 +673,7 @@ int32_t nca_b200_state_bytes(int32_t n_inst, int32_t hw, int32_t channels, int32
   const bool hl = hilo_layout(channels, precision == NCA_PREC_BF16);
   const size_t master = align256((size_t)tiles * kTileM * channels * (hl ? 2 : 4));
   const size_t mirror = precision == NCA_PREC_BF16 ? align256((size_t)tiles * kTileM * channels * 2) : 0;
-  *bytes = 2 * master + 2 * mirror;
+  *bytes = 2 * master + 2 * mirror + align256((size_t)tiles * 4);  // + per-tile step counters
   return NCA_OK;
 }
 
@@ -688,6 +699,7 @@ int32_t nca_b200_state_bind(NcaState* st, void* buffer, size_t bytes, int32_t n_
   st->master[1] = reinterpret_cast<float*>(p + master);
   st->mirror[0] = mirror ? reinterpret_cast<uint16_t*>(p + 2 * master) : nullptr;
   st->mirror[1] = mirror ? reinterpret_cast<uint16_t*>(p + 2 * master + mirror) : nullptr;
+  st->tile_steps = reinterpret_cast<uint32_t*>(p + 2 * master + 2 * mirror);
   st->cur = 0;
   st->clamped = 0;
   return NCA_OK;

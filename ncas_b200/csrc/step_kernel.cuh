@@ -44,10 +44,12 @@ constexpr int pow2ceil(int v) {
 // cell), else an fp32 master plus a bf16 mirror for the stencil; split mode keeps fp32.
 __host__ __device__ constexpr bool hilo_layout(int C, bool bf16) { return bf16 && C >= 64; }
 
-template <int C_, int HD_, bool SPLIT_, bool NOISE_ = false>
+template <int C_, int HD_, bool SPLIT_, bool NOISE_ = false, bool TILEDEP_ = false>
 struct StepCfg {
   static constexpr int C = C_;
   static constexpr bool NOISE = NOISE_;  // test-time state noise (a separate instantiation)
+  // steps ordered by per-tile step counters (StepArgs::tile_steps) instead of a grid barrier
+  static constexpr bool TILEDEP = TILEDEP_;
   static constexpr int P = 4 * C_;
   static constexpr int HD = HD_;
   static constexpr bool SPLIT = SPLIT_;
@@ -129,6 +131,7 @@ struct StepArgs {
   float noise_p_t, noise_p_s, noise_sigma;
   long long noise_until;
   const float* noise;
+  unsigned* tile_steps;  // per tile: steps of this launch whose stores are complete (TILEDEP)
   int* ctrl;
   unsigned long long timeout_ns;
 };
@@ -153,6 +156,11 @@ struct SmemLayout {
 };
 
 constexpr int kMaxStages = 4;  // window stages
+#ifndef NCA_TILEDEP_PER_CTA
+#define NCA_TILEDEP_PER_CTA 8
+#endif
+// launches with at most this many tiles per CTA order their steps by per-tile step counters
+constexpr int kTileDepPerCta = NCA_TILEDEP_PER_CTA;
 enum BarId {
   BAR_WIN_FULL = 0,   // +stage (4)
   BAR_WIN_EMPTY = 4,  // +stage (4)
@@ -173,7 +181,7 @@ enum BarId {
 // Failure sites reported in ctrl[1].
 enum Where {
   W_MMA_ZFULL = 1, W_MMA_ACCEMPTY, W_MMA_HFULL, W_MMA_WEIGHTS, W_LOAD_EMPTY, W_LOAD_GRID,
-  W_ST_WINFULL, W_ST_ZEMPTY, W_E1_ACC, W_E2_ACC2, W_DRAIN, W_E2_FLAGS
+  W_ST_WINFULL, W_ST_ZEMPTY, W_E1_ACC, W_E2_ACC2, W_DRAIN, W_E2_FLAGS, W_PUBLISH
 };
 
 // A window stage is laid out [chunk][window cell][16 B]: lanes that read the same chunk of
@@ -326,7 +334,8 @@ __device__ __forceinline__ void head_readout(int kind, int n_out, int c_out, con
 // cell's fp32 state): the continuous rule p = scale * (1 - conf) + bias, or the reference's
 // threshold rule (src/nca/model.py:566-593) p = p_low for confident cells (conf > tau, or given
 // cells when given_confident), else p_fire; fire when u < p with u from Philox or the caller.
-// Read from the fp32 state of the step's input buffer (complete since the last grid barrier).
+// Read from the state of the step's input buffer (the cell's own tile has stored step s-1: the
+// loader waited for it before loading the tile's window).
 // xhi: in the hi/lo layout, the hi parts of the readout slice (read from the window stage by
 // the caller while the stage is still its own); the lo parts come from global memory.
 template <class Cfg>
@@ -370,6 +379,8 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L.misc);
   int* abort_flag = reinterpret_cast<int*>(smem + L.misc + 8);
+  // epilogue warps that have stored a tile (8 per tile), read by the publisher lane
+  unsigned* s_tiles_done = reinterpret_cast<unsigned*>(smem + L.misc + 16);
   float* s_b1 = reinterpret_cast<float*>(smem + L.b1);
   float* s_b2 = reinterpret_cast<float*>(smem + L.b2);
   uint8_t* s_flags = smem + L.flags;  // [4][128]: bit0 fire, bit1 given, bit2 valid
@@ -385,6 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
+    *s_tiles_done = 0;
     for (int s = 0; s < kMaxStages; ++s) {
       mbar_init(&bars[BAR_WIN_FULL + s], 1);
       // released by the 8 stencil warps, or in bf16 mode by the 8 epilogue warps, which read
@@ -441,6 +453,41 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
 
   if (!skip && warp == 0) {
     // ---------------------------------------------------------------- MMA issuer
+    if (Cfg::TILEDEP && lane == 1 && A.n_steps > 1) {
+      // ------------------------------------------------------------ publisher
+      // In tile order: once the 8 epilogue warps have stored tile t of step s, a gpu-scope
+      // fence (cumulative over those stores, acquired at CTA scope) and the tile's counter
+      // tile_steps[t] = s + 1, which the loaders of neighbouring tiles wait for.
+      long long it = 0;
+      bool ok = true;
+      for (int s = 0; ok && s + 1 < A.n_steps; ++s) {
+        for (long long t = blockIdx.x; t < A.n_tiles; t += grid, ++it) {
+          const unsigned want = 8u * (unsigned)(it + 1);
+          uint64_t start = 0;
+          for (uint32_t k = 0;; ++k) {
+            unsigned v;
+            asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(s_tiles_done)) : "memory");
+            if (v >= want) break;
+            if ((k & 63) == 63) {
+              const uint64_t now = global_timer_ns();
+              if (start == 0) start = now;
+              if (should_abort(fs)) { ok = false; break; }
+              if (now - start > fs.timeout_ns || k > (1u << 28)) {
+                report_failure(fs, 4, W_PUBLISH);
+                ok = false;
+                break;
+              }
+            }
+            __nanosleep(32);
+          }
+          if (!ok) break;
+          __threadfence();
+          asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(A.tile_steps + t), "r"((unsigned)(s + 1)) : "memory");
+        }
+        // this CTA has stored every tile of step s
+        if (ok) atomicAdd(reinterpret_cast<unsigned*>(A.ctrl + 2), 1u);
+      }
+    }
     if (lane == 0) {
       bool ok = true;
       // weights are loaded by the loader warp
@@ -556,11 +603,12 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
     const int S = A.stages;
     long long it = 0;
     bool ok = true;
+    int done_step = 0;  // every tile has stored the steps before done_step
     for (int s = 0; ok && s < A.n_steps; ++s) {
       const int in = (A.cur + s) & 1;
       const uint8_t* src = Cfg::SRC_BF16 ? reinterpret_cast<const uint8_t*>(A.mirror[in])
                                          : reinterpret_cast<const uint8_t*>(A.master[in]);
-      if (s > 0) {
+      if (!Cfg::TILEDEP && s > 0) {
         // grid barrier: every CTA has stored its tiles of step s-1
         int give_up = 0;
         if (lane == 0) {
@@ -588,6 +636,48 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         const long long wb = t * kTileM - W - 1;
         const long long lo = wb < 0 ? 0 : wb;
         const long long hi = (wb + WC) < total ? (wb + WC) : total;
+        if (Cfg::TILEDEP && s > 0 && done_step < s) {
+          // Per-tile dependencies instead of a grid barrier: the window reads step s-1 of the
+          // tiles it overlaps, so each of them must have stored step s-1 (their counters reach s).
+          // The same condition orders this tile's later stores into the other buffer after
+          // those tiles' reads of it at step s-1.  One lane per overlapped tile, bounded; lane 31
+          // also reads the count of CTAs that finished step s-1 (ctrl[2]), and once every CTA
+          // has, the rest of the step needs no checks.
+          const long long T = (lo >> 7) + lane;
+          bool need = T <= ((hi - 1) >> 7);
+          uint64_t start = 0;
+          for (uint32_t k = 0;; ++k) {
+            if (need) {
+              unsigned v;
+              asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(A.tile_steps + T) : "memory");
+              need = v < (unsigned)s;
+            }
+            unsigned all = 0;
+            if (lane == 31) {
+              unsigned v;
+              asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(A.ctrl + 2) : "memory");
+              all = v >= (unsigned)s * (unsigned)grid ? 1u : 0u;
+            }
+            if (__shfl_sync(0xffffffffu, all, 31)) {
+              done_step = s;
+              break;
+            }
+            if (!__any_sync(0xffffffffu, need)) break;
+            int give_up = 0;
+            if (lane == 0 && (k & 15) == 15) {
+              const uint64_t now = global_timer_ns();
+              if (start == 0) start = now;
+              if (should_abort(fs)) give_up = 1;
+              else if (now - start > fs.timeout_ns || k > (1u << 28)) {
+                report_failure(fs, 4, W_LOAD_GRID);
+                give_up = 1;
+              }
+            }
+            if (__shfl_sync(0xffffffffu, give_up, 0)) { ok = false; break; }
+            __nanosleep(64);
+          }
+          if (!ok) break;
+        }
         if (lane == 0) mbar_arrive_expect_tx(&bars[BAR_WIN_FULL + stage], (uint32_t)(NCH * (hi - lo) * 16));
         __syncwarp();
         const uint32_t dst = smem_u32(smem + L.win + stage * (WC + 1) * Cfg::ROWB);
@@ -1034,22 +1124,30 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
             if (cnt) atomicAdd(&A.updates[inst], (unsigned)cnt);
           }
         }
+        if constexpr (Cfg::TILEDEP) {
+          // this warp's stores of the tile are issued: count it for the publisher lane (the warp
+          // barrier orders the lanes' stores before lane 0's release)
+          __syncwarp();
+          if (lane == 0) asm volatile("red.release.cta.shared::cta.add.u32 [%0], 1;" ::"r"(smem_u32(s_tiles_done)) : "memory");
+        }
       }
-      // Step done: this CTA's stores of step s are complete.  The barrier also ORs the failure
-      // flags of the 8 epilogue warps so that they leave the step loop together.
-      unsigned any_fail;
-      asm volatile(
-          "{\n\t.reg .pred p, q;\n\t"
-          "setp.ne.u32 p, %1, 0;\n\t"
-          "bar.red.or.pred q, 1, 256, p;\n\t"
-          "selp.u32 %0, 1, 0, q;\n\t}"
-          : "=r"(any_fail)
-          : "r"((unsigned)(!ok || *(volatile int*)abort_flag != 0))
-          : "memory");
-      if (any_fail) { ok = false; break; }
-      if (threadIdx.x == kEpiWarp0 * 32) {
-        __threadfence();
-        atomicAdd(reinterpret_cast<unsigned*>(&A.ctrl[2]), 1u);
+      if constexpr (!Cfg::TILEDEP) {
+        // Step done: this CTA's stores of step s are complete.  The barrier also ORs the failure
+        // flags of the 8 epilogue warps so that they leave the step loop together.
+        unsigned any_fail;
+        asm volatile(
+            "{\n\t.reg .pred p, q;\n\t"
+            "setp.ne.u32 p, %1, 0;\n\t"
+            "bar.red.or.pred q, 1, 256, p;\n\t"
+            "selp.u32 %0, 1, 0, q;\n\t}"
+            : "=r"(any_fail)
+            : "r"((unsigned)(!ok || *(volatile int*)abort_flag != 0))
+            : "memory");
+        if (any_fail) { ok = false; break; }
+        if (threadIdx.x == kEpiWarp0 * 32) {
+          __threadfence();
+          atomicAdd(reinterpret_cast<unsigned*>(&A.ctrl[2]), 1u);
+        }
       }
     }
   }

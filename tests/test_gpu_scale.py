@@ -105,6 +105,29 @@ def test_none_and_all_given(fraction):
     assert_given_cells_keep_clamp(x0, x, given, 3, 0, 10)
 
 
+@pytest.mark.parametrize("task,n_small,K,n_big", [("sudoku", 16, 8, 320), ("maze", 8, 4, 240)])
+def test_step_ordering_by_tile_counters_equals_grid_barrier(task, n_small, K, n_big):
+    """A launch with few tiles per CTA orders its steps by per-tile step counters, a larger one by
+    a grid barrier.  The same instances stepped in both (the small batch, then the same boards at
+    the front of a batch of more than 8 tiles per SM) give bit-identical states."""
+    if task == "sudoku":
+        from ncas_b200.tasks import sudoku_boards
+
+        boards = sudoku_boards(n_small, seed=4)
+    else:
+        boards = maze_boards(n_small, 13, seed=4)
+    reps = -(-n_big // n_small)
+    big_in = np.concatenate([boards.inputs] * reps)[:n_big]
+    big_g = np.concatenate([boards.given] * reps)[:n_big]
+    hw = boards.inputs.shape[1] * boards.inputs.shape[2]
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert -(-n_small * K * hw // 128) <= 8 * sms < -(-n_big * K * hw // 128)
+    _, _, xa, ua = run_philox(task, "bf16", boards.inputs, boards.given, K, 12, seed=8)
+    _, _, xb, ub = run_philox(task, "bf16", big_in, big_g, K, 12, seed=8)
+    n = n_small * K
+    assert torch.equal(xa, xb[:n]) and torch.equal(ua, ub[:n])
+
+
 @pytest.mark.parametrize("precision", ["bf16", "split"])
 def test_full_cfg2_batch_sampled_instances_match_oracle(precision):
     bc = CONFIGS["cfg2"]  # 1000 sudoku boards x 128 trials

@@ -75,9 +75,10 @@ def test_state_bytes(lib):
     tiles = -(-1000 * 81 // 128)
     lo = tiles * 128 * 64 * 2  # bf16 mode: hi (mirror) and lo bf16 arrays, two buffers each
     hi = tiles * 128 * 64 * 2
-    assert n.value == 2 * lo + 2 * hi
+    flags = (tiles * 4 + 255) & ~255  # per-tile step counters
+    assert n.value == 2 * lo + 2 * hi + flags
     assert lib.nca_b200_state_bytes(10, 81, 64, L.PREC_SPLIT, C.byref(n)) == 0
-    assert n.value == 2 * (-(-810 // 128) * 128 * 64 * 4 + 255 & ~255)
+    assert n.value == 2 * (-(-810 // 128) * 128 * 64 * 4 + 255 & ~255) + 256
     assert lib.nca_b200_state_bytes(0, 81, 64, 0, C.byref(n)) == 1
 
 

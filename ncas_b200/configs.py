@@ -56,6 +56,17 @@ class BenchConfig:
         P = 4 * C
         return 2 * (P * P + P * C)
 
+    def bytes_per_cell_update(self, precision: str = "bf16") -> int:
+        """Algorithmic HBM bytes of one cell-update of the step kernel.  bf16 mode with C >= 64
+        keeps the state as bf16 hi + lo parts: the window reads hi (2C), the epilogue reads lo
+        (2C) and writes both (4C) = 8C.  Otherwise the window reads the bf16 mirror (2C; fp32
+        in split mode, 4C), the epilogue reads the fp32 state (4C) and writes it (4C) plus the
+        mirror (2C in bf16 mode) = 12C."""
+        C = self.channels
+        if precision == "bf16":
+            return 8 * C if C >= 64 else 12 * C
+        return 12 * C
+
     @property
     def cell_updates(self) -> int:
         return self.n_boards * self.k * self.hw * self.depth

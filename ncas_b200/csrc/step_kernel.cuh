@@ -64,15 +64,18 @@ struct StepCfg {
   static constexpr int SLOT_COLS = ZPARTS * KMAX / 2;
   static constexpr int NZ = (2 * SLOT_COLS + HD <= 512) ? 2 : 1;
   static constexpr int ACC_COL = NZ * SLOT_COLS;
-  static constexpr int TMEM_COLS = pow2ceil(ACC_COL + HD);
   // bf16 mode keeps h in the accumulator region (each epilogue thread overwrites the columns it
   // has read), so a z slot is free as soon as GEMM1 is done; acc2 then sits in columns
   // [HD/4, HD/2) of the region.  Split mode writes h (hi and lo) over the consumed z slot.
   static constexpr bool H_IN_ACC = !SPLIT_;
+  // Accumulator regions (HD columns each, tile it uses region it % NACC).  Two fit beside the z
+  // slots when HD <= 128: GEMM1 of the next tile then runs while the epilogue finishes this one.
+  static constexpr int NACC = (H_IN_ACC && ACC_COL + 2 * HD <= 512) ? 2 : 1;
+  static constexpr int TMEM_COLS = pow2ceil(ACC_COL + NACC * HD);
   static constexpr int ACC2_COL = ACC_COL + (H_IN_ACC ? HD / 4 : 0);
   static constexpr int W1_BYTES = HD * P * 2;
   static constexpr int W2_BYTES = C * HD * 2;
-  static_assert(ACC_COL + HD <= 512, "tensor memory budget");
+  static_assert(ACC_COL + NACC * HD <= 512, "tensor memory budget");
   static_assert(C % 16 == 0 && HD % 32 == 0 && HD <= 256 && P % 64 == 0 && HD % 64 == 0,
                 "shape constraints of the UMMA tiles");
   static_assert(NCH % 2 == 0, "stencil channel halves");
@@ -150,7 +153,7 @@ struct SmemLayout {
     b2 = b1 + Cfg::HD * 4;
     flags = b2 + Cfg::C * 4;
     bars = (flags + 4 * kTileM + 7) & ~7;
-    misc = bars + 24 * 8;  // BAR_COUNT <= 24 barriers
+    misc = bars + 32 * 8;  // BAR_COUNT <= 32 barriers
     total = misc + 64;
   }
 };
@@ -166,17 +169,19 @@ enum BarId {
   BAR_WIN_EMPTY = 4,  // +stage (4)
   BAR_Z_FULL = 8,     // +slot (2)
   BAR_Z_EMPTY = 10,   // +slot (2)
-  BAR_ACC_FULL = 12,
-  BAR_H_FULL = 13,
-  BAR_ACC2_FULL = 14,
-  BAR_ACC_EMPTY = 15,
-  BAR_WEIGHTS = 16,
-  BAR_DRAIN = 17,
-  BAR_ACC_FULL_B = 18,  // second half of GEMM1 (hidden units HD/2 .. HD)
-  BAR_H_FULL_B = 19,    // second half of the hidden epilogue
-  BAR_FLAGS = 20,       // +ring index (4): per-row fire/given flags of a tile are written
-  BAR_COUNT = 24
+  // +accumulator region (2) each:
+  BAR_ACC_FULL = 12,    // first half of GEMM1 (hidden units 0 .. HD/2)
+  BAR_ACC_FULL_B = 14,  // second half of GEMM1 (hidden units HD/2 .. HD)
+  BAR_H_FULL = 16,      // first half of the hidden epilogue
+  BAR_H_FULL_B = 18,    // second half of the hidden epilogue
+  BAR_ACC2_FULL = 20,   // GEMM2
+  BAR_ACC_EMPTY = 22,   // acc2 read: the region is free
+  BAR_WEIGHTS = 24,
+  BAR_DRAIN = 25,
+  BAR_FLAGS = 26,       // +ring index (4): per-row fire/given flags of a tile are written
+  BAR_COUNT = 30
 };
+static_assert(BAR_COUNT <= 32, "barrier area of the shared-memory layout");
 
 // Failure sites reported in ctrl[1].
 enum Where {
@@ -407,12 +412,14 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
       mbar_init(&bars[BAR_Z_FULL + s], 8);
       mbar_init(&bars[BAR_Z_EMPTY + s], 1);
     }
-    mbar_init(&bars[BAR_ACC_FULL], 1);
-    mbar_init(&bars[BAR_ACC_FULL_B], 1);
-    mbar_init(&bars[BAR_H_FULL], 4);
-    mbar_init(&bars[BAR_H_FULL_B], 4);
-    mbar_init(&bars[BAR_ACC2_FULL], 1);
-    mbar_init(&bars[BAR_ACC_EMPTY], 8);
+    for (int r = 0; r < 2; ++r) {
+      mbar_init(&bars[BAR_ACC_FULL + r], 1);
+      mbar_init(&bars[BAR_ACC_FULL_B + r], 1);
+      mbar_init(&bars[BAR_H_FULL + r], 4);
+      mbar_init(&bars[BAR_H_FULL_B + r], 4);
+      mbar_init(&bars[BAR_ACC2_FULL + r], 1);
+      mbar_init(&bars[BAR_ACC_EMPTY + r], 8);
+    }
     mbar_init(&bars[BAR_WEIGHTS], 1);
     mbar_init(&bars[BAR_DRAIN], 1);
     for (int r = 0; r < 4; ++r) mbar_init(&bars[BAR_FLAGS + r], 4);
@@ -515,8 +522,12 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           const int slot = (int)(it % Cfg::NZ);
           const uint32_t u = (uint32_t)(it / Cfg::NZ);
           const uint32_t zcol = tmem + slot * Cfg::SLOT_COLS;
+          const int rg = (int)(it % Cfg::NACC);             // accumulator region
+          const uint32_t ua = (uint32_t)(it / Cfg::NACC) & 1;  // its phase
+          const uint32_t acol = tmem + Cfg::ACC_COL + rg * Cfg::HD;
+          const uint32_t a2col = acol + (Cfg::ACC2_COL - Cfg::ACC_COL);
           if (!mbar_wait(&bars[BAR_Z_FULL + slot], u & 1, fs, W_MMA_ZFULL)) { ok = false; break; }
-          if (!mbar_wait(&bars[BAR_ACC_EMPTY], ((uint32_t)it & 1) ^ 1, fs, W_MMA_ACCEMPTY)) { ok = false; break; }
+          if (!mbar_wait(&bars[BAR_ACC_EMPTY + rg], ua ^ 1, fs, W_MMA_ACCEMPTY)) { ok = false; break; }
           tc_fence_after();
           // GEMM1 in two N halves (hidden units [0, HD/2) then [HD/2, HD)).  In bf16 mode each half
           // is committed on its own, so that the hidden epilogue of the first half overlaps the
@@ -530,43 +541,41 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
               const uint32_t boff = (kk >> 2) * (Cfg::HD * 128) + nh * (Cfg::HD / 2) * 128 + (kk & 3) * 32;
 #pragma unroll
               for (int part = 0; part < Cfg::ZPARTS; ++part)
-                umma_bf16_ts(tmem + Cfg::ACC_COL + nh * (Cfg::HD / 2), zcol + part * (Cfg::P / 2) + kk * 8,
+                umma_bf16_ts(acol + nh * (Cfg::HD / 2), zcol + part * (Cfg::P / 2) + kk * 8,
                              desc_add(d1, boff), id1, (kk | part) != 0);
               if (Cfg::SPLIT && wlo)
-                umma_bf16_ts(tmem + Cfg::ACC_COL + nh * (Cfg::HD / 2), zcol + kk * 8, desc_add(d1lo, boff),
-                             id1, 1u);
+                umma_bf16_ts(acol + nh * (Cfg::HD / 2), zcol + kk * 8, desc_add(d1lo, boff), id1, 1u);
             }
-            if (Cfg::H_IN_ACC) umma_commit(&bars[nh == 0 ? BAR_ACC_FULL : BAR_ACC_FULL_B]);
+            if (Cfg::H_IN_ACC) umma_commit(&bars[(nh == 0 ? BAR_ACC_FULL : BAR_ACC_FULL_B) + rg]);
           }
           if (Cfg::H_IN_ACC) {
             umma_commit(&bars[BAR_Z_EMPTY + slot]);
           } else {
-            umma_commit(&bars[BAR_ACC_FULL]);
-            umma_commit(&bars[BAR_ACC_FULL_B]);
+            umma_commit(&bars[BAR_ACC_FULL + rg]);
+            umma_commit(&bars[BAR_ACC_FULL_B + rg]);
           }
           // GEMM2 in two K halves, each as soon as its half of h is in tensor memory.
 #pragma unroll
           for (int kh = 0; kh < 2; ++kh) {
-            if (!mbar_wait(&bars[kh == 0 ? BAR_H_FULL : BAR_H_FULL_B], (uint32_t)it & 1, fs, W_MMA_HFULL)) { ok = false; break; }
+            if (!mbar_wait(&bars[(kh == 0 ? BAR_H_FULL : BAR_H_FULL_B) + rg], ua, fs, W_MMA_HFULL)) { ok = false; break; }
             tc_fence_after();
 #pragma unroll
             for (int kq = 0; kq < Cfg::HD / 32; ++kq) {
               const int kk = kh * (Cfg::HD / 32) + kq;
               const uint32_t boff = (kk >> 2) * (Cfg::C * 128) + (kk & 3) * 32;
               if constexpr (Cfg::H_IN_ACC) {
-                umma_bf16_ts(tmem + Cfg::ACC2_COL, tmem + Cfg::ACC_COL + kh * (Cfg::HD / 2) + kq * 8,
-                             desc_add(d2, boff), id2, kk != 0);
+                umma_bf16_ts(a2col, acol + kh * (Cfg::HD / 2) + kq * 8, desc_add(d2, boff), id2, kk != 0);
               } else {
 #pragma unroll
                 for (int part = 0; part < Cfg::ZPARTS; ++part)
-                  umma_bf16_ts(tmem + Cfg::ACC2_COL, zcol + part * (Cfg::HD / 2) + kk * 8, desc_add(d2, boff),
-                               id2, (kk | part) != 0);
-                if (wlo) umma_bf16_ts(tmem + Cfg::ACC2_COL, zcol + kk * 8, desc_add(d2lo, boff), id2, 1u);
+                  umma_bf16_ts(a2col, zcol + part * (Cfg::HD / 2) + kk * 8, desc_add(d2, boff), id2,
+                               (kk | part) != 0);
+                if (wlo) umma_bf16_ts(a2col, zcol + kk * 8, desc_add(d2lo, boff), id2, 1u);
               }
             }
           }
           if (!ok) break;
-          umma_commit(&bars[BAR_ACC2_FULL]);
+          umma_commit(&bars[BAR_ACC2_FULL + rg]);
           if (!Cfg::H_IN_ACC) umma_commit(&bars[BAR_Z_EMPTY + slot]);
         }
       }
@@ -897,7 +906,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           mbar_arrive_relaxed(&bars[BAR_Z_FULL + slot]);
           // hi/lo layout: the epilogue still reads the tile's own cells (the hi part of the old
           // state) from this window and releases it
-          if constexpr (!Cfg::HILO) mbar_arrive_relaxed(&bars[BAR_WIN_EMPTY + stage]);
+          if constexpr (!Cfg::HILO) mbar_arrive(&bars[BAR_WIN_EMPTY + stage]);
         }
         if (half == 0 && A.fire_mode >= 2) {
           // adaptive rules: the fire decision needs the confidence of the cell's fp32 state; it
@@ -934,7 +943,9 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
       for (long long t = blockIdx.x; t < A.n_tiles; t += grid, ++it) {
         const int slot = (int)(it % Cfg::NZ);
         const uint32_t zbase = tmem + lane_addr + slot * Cfg::SLOT_COLS;
-        const uint32_t abase = tmem + lane_addr + Cfg::ACC_COL;
+        const int rg = (int)(it % Cfg::NACC);             // accumulator region of the tile
+        const uint32_t ua = (uint32_t)(it / Cfg::NACC) & 1;  // its phase
+        const uint32_t abase = tmem + lane_addr + Cfg::ACC_COL + rg * Cfg::HD;
         // ---- before E1: index math; the fire and given flags come from the stencil warps
         // (s_flags).
         const unsigned g = (unsigned)t * kTileM + m;
@@ -944,7 +955,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         constexpr int NQ = CH / 4;  // float4 chunks of this thread
         const float4* xin4 = reinterpret_cast<const float4*>(xin) + ((t * (Cfg::C / 4) + half * NQ) << 7) + m;
         // ---- E1: hidden = relu(acc1 + b1) -> bf16 into the z slot
-        if (!warp_wait(&bars[half == 0 ? BAR_ACC_FULL : BAR_ACC_FULL_B], (uint32_t)it & 1, fs, W_E1_ACC)) { ok = false; break; }
+        if (!warp_wait(&bars[(half == 0 ? BAR_ACC_FULL : BAR_ACC_FULL_B) + rg], ua, fs, W_E1_ACC)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll 1
         for (int cbk = 0; cbk < Cfg::HD / 2; cbk += 32) {
@@ -980,7 +991,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_relaxed(&bars[half == 0 ? BAR_H_FULL : BAR_H_FULL_B]);
+        if (lane == 0) mbar_arrive_relaxed(&bars[(half == 0 ? BAR_H_FULL : BAR_H_FULL_B) + rg]);
 
         // ---- E2: dx = acc2 + b2; x' = x + f * dx; clamp; store.  The old state of this thread's
         // channels is loaded while GEMM2 runs.
@@ -1003,7 +1014,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           // the stencil warps finished every read of this window before handing z to the MMA
           // warp, and this warp has its hi values: release the stage to the loader
           __syncwarp();
-          if (lane == 0) mbar_arrive_relaxed(&bars[BAR_WIN_EMPTY + (int)(it % A.stages)]);
+          if (lane == 0) mbar_arrive(&bars[BAR_WIN_EMPTY + (int)(it % A.stages)]);
         } else {
 #pragma unroll
           for (int q = 0; q < NQ; ++q) xo[q] = valid ? __ldg(xin4 + (q << 7)) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -1013,7 +1024,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         const uint32_t fl = s_flags[(it & 3) * kTileM + m];
         const bool gv = (fl & 2u) != 0;
         const float f = (fl & 1u) ? 1.f : 0.f;
-        if (!warp_wait(&bars[BAR_ACC2_FULL], (uint32_t)it & 1, fs, W_E2_ACC2)) { ok = false; break; }
+        if (!warp_wait(&bars[BAR_ACC2_FULL + rg], ua, fs, W_E2_ACC2)) { ok = false; break; }
         tc_fence_after();
         uint32_t r[CH];
         if constexpr (CH == 32) {
@@ -1027,7 +1038,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         tc_wait_ld_regs(r);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_relaxed(&bars[BAR_ACC_EMPTY]);
+        if (lane == 0) mbar_arrive_relaxed(&bars[BAR_ACC_EMPTY + rg]);
         if (valid) {
           const float4* bb = reinterpret_cast<const float4*>(s_b2 + half * CH);
           const float2 ff = f2(f, f);

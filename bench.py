@@ -5,7 +5,8 @@
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N
     python bench.py --impl reference      # the CPU restatement of the reference, host cores
 
-One bench step = one complete rollout of the workload's boards on this rank's shard: state
+One bench step = one complete rollout of the workload's boards on every rank (weak scaling:
+rank r runs its own boards as boards [r * n, (r + 1) * n) of an N-times larger job): state
 init, `depth` NCA steps for K trials per board (the persistent tcgen05 step kernel; pruning /
 adaptive firing as the workload says), readout and conf@K selection, and for N > 1 the
 all-gather of the per-board results.  Inputs are resident in HBM; e2e repeats the step through
@@ -166,7 +167,7 @@ def run_ours(args) -> None:
     import torch.distributed as dist
 
     from ncas_b200.configs import CONFIGS, boards_for, build, task_for
-    from ncas_b200.distributed import gather_results, shard_range
+    from ncas_b200.distributed import gather_results
     from ncas_b200.rollout import RolloutConfig, rollout
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -188,9 +189,12 @@ def run_ours(args) -> None:
         bc = dataclasses.replace(bc, n_boards=args.boards or bc.n_boards, depth=args.depth or bc.depth)
     model = build(bc.task, seed=0, device=dev, precision=args.precision)
     eng = model.engine()
-    boards = boards_for(bc, seed=0)
-    s, e = shard_range(bc.n_boards, world, rank)
-    shard = boards.subset(np.arange(s, e))
+    # Weak scaling: every rank runs the workload's full board count on boards of its own (seed =
+    # rank; rank 0's are the one-GPU boards), as global boards [rank * n, (rank + 1) * n) of an
+    # N-times larger job, so the Philox streams of all ranks are distinct.
+    n_total = bc.n_boards * world
+    s = rank * bc.n_boards
+    shard = boards_for(bc, seed=rank)
     n, K, HW = len(shard), bc.k, bc.hw
     batch = eng.batch_from_boards(shard.inputs, shard.given, K, inst_offset=s * K)
     st = eng.new_state(n * K, HW)
@@ -218,7 +222,7 @@ def run_ours(args) -> None:
         r = eng.readout(st, batch)
         idx, best, bp = eng.select(r["board_conf"], n, K, pred=r["pred"], hw=HW)
         if world > 1:
-            gather_results(best, idx, bp, bc.n_boards)
+            gather_results(best, idx, bp, n_total)
         return best
 
     def barrier():
@@ -248,7 +252,7 @@ def run_ours(args) -> None:
     if world > 1:
         dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
     ms = float(t_max.item())
-    total_cu = bc.cell_updates * args.steps  # all ranks' boards
+    total_cu = bc.cell_updates * world * args.steps  # all ranks' boards
     value = total_cu / (ms / 1e3)
 
     # ---- e2e through the public API (host boards in, host results out)
@@ -269,7 +273,7 @@ def run_ours(args) -> None:
         e2e_s = torch.tensor([time.perf_counter() - w0], device=dev)
         if world > 1:
             dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
-        e2e_value = bc.cell_updates * e2e_steps / float(e2e_s.item())
+        e2e_value = bc.cell_updates * world * e2e_steps / float(e2e_s.item())
         h2d = int(shard.inputs.nbytes + shard.given.nbytes + shard.targets.nbytes)
         d2h = int(res.pred.size + res.conf.nbytes + res.cell_updates.nbytes)
 
@@ -300,7 +304,8 @@ def run_ours(args) -> None:
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if args.precision == "bf16" else "bf16x2",
             "data": "synthetic",
-            "config": {"workload": bc.name, "boards": bc.n_boards, "k": K, "depth": bc.depth,
+            "config": {"workload": bc.name, "boards": n_total, "boards_per_gpu": bc.n_boards, "k": K,
+                       "depth": bc.depth,
                        "hw": HW, "task": bc.task, "parallelism": f"boards sharded over {world} GPU(s)",
                        "l2": f"state {st.buffer.numel() / 1e9:.1f} GB > 126 MB L2 (inputs larger than L2)"},
             "roofline": roof,

@@ -564,7 +564,7 @@ int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaState* st,
   // cost is then small against the step (the per-tile form costs the epilogue registers and the
   // MMA warp a publisher lane).
   const bool tiledep = n_steps > 1 && A.n_tiles <= (long long)kTileDepPerCta * grid;
-  using CfgTD = StepCfg<Cfg::C, Cfg::HD, Cfg::SPLIT, Cfg::NOISE, true>;
+  using CfgTD = StepCfg<Cfg::C, Cfg::HD, Cfg::SPLIT, Cfg::NOISE, true, Cfg::ADAPTIVE>;
   auto kern = tiledep ? nca_step_kernel<CfgTD> : nca_step_kernel<Cfg>;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return NCA_ERR_CUDA;
@@ -760,14 +760,19 @@ int32_t nca_b200_run_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaStat
   if (fire->noise_mode < 0 || fire->noise_mode > 2) return NCA_ERR_INVALID;
   if (fire->noise_mode == NCA_NOISE_EXTERNAL && (!fire->noise || n_steps != 1)) return NCA_ERR_INVALID;
   const bool noise = fire->noise_mode != NCA_NOISE_NONE;
+  const bool adaptive = fire->mode >= NCA_FIRE_ADAPTIVE_PHILOX;  // fire decisions on the confidence
   auto launch = [&](int32_t n, const NcaFireDesc* f) -> int32_t {
-#define NCA_LAUNCH(CC, HH)                                                                          \
-  if (C == CC && HD == HH) {                                                                        \
-    if (noise)                                                                                      \
-      return split ? launch_steps<StepCfg<CC, HH, true, true>>(m, b, st, n, f, ctrl, timeout_ms, s)  \
-                   : launch_steps<StepCfg<CC, HH, false, true>>(m, b, st, n, f, ctrl, timeout_ms, s); \
-    return split ? launch_steps<StepCfg<CC, HH, true>>(m, b, st, n, f, ctrl, timeout_ms, s)          \
-                 : launch_steps<StepCfg<CC, HH, false>>(m, b, st, n, f, ctrl, timeout_ms, s);        \
+#define NCA_LAUNCH_AD(CC, HH, SP, NZ)                                                             \
+  return adaptive ? launch_steps<StepCfg<CC, HH, SP, NZ, false, true>>(m, b, st, n, f, ctrl, timeout_ms, s) \
+                  : launch_steps<StepCfg<CC, HH, SP, NZ>>(m, b, st, n, f, ctrl, timeout_ms, s);
+#define NCA_LAUNCH(CC, HH)                                                                        \
+  if (C == CC && HD == HH) {                                                                      \
+    if (noise) {                                                                                  \
+      if (split) { NCA_LAUNCH_AD(CC, HH, true, true) }                                            \
+      NCA_LAUNCH_AD(CC, HH, false, true)                                                          \
+    }                                                                                             \
+    if (split) { NCA_LAUNCH_AD(CC, HH, true, false) }                                             \
+    NCA_LAUNCH_AD(CC, HH, false, false)                                                           \
   }
     // the benchmark models (32, 128), (64, 256) and the reference's maze presets (16, 128),
     // (32, 256) (maze_ood, maze_hard: src/nca/model.py:656-700)
@@ -776,6 +781,7 @@ int32_t nca_b200_run_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaStat
     NCA_LAUNCH(16, 128)
     NCA_LAUNCH(32, 256)
 #undef NCA_LAUNCH
+#undef NCA_LAUNCH_AD
     return NCA_ERR_UNSUPPORTED;
   };
   if (st->clamped) return launch(n_steps, fire);

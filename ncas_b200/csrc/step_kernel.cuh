@@ -44,10 +44,14 @@ constexpr int pow2ceil(int v) {
 // cell), else an fp32 master plus a bf16 mirror for the stencil; split mode keeps fp32.
 __host__ __device__ constexpr bool hilo_layout(int C, bool bf16) { return bf16 && C >= 64; }
 
-template <int C_, int HD_, bool SPLIT_, bool NOISE_ = false, bool TILEDEP_ = false>
+template <int C_, int HD_, bool SPLIT_, bool NOISE_ = false, bool TILEDEP_ = false,
+          bool ADAPTIVE_ = false>
 struct StepCfg {
   static constexpr int C = C_;
   static constexpr bool NOISE = NOISE_;  // test-time state noise (a separate instantiation)
+  // fire decisions on the cell's confidence (fire modes 2..5), evaluated by all 8 stencil warps
+  // after z; the other modes draw them in the half-0 stencil warps before z
+  static constexpr bool ADAPTIVE = ADAPTIVE_;
   // steps ordered by per-tile step counters (StepArgs::tile_steps) instead of a grid barrier
   static constexpr bool TILEDEP = TILEDEP_;
   static constexpr int P = 4 * C_;
@@ -315,11 +319,12 @@ __device__ __forceinline__ void head_readout(int kind, int n_out, int c_out, con
   };
   float best = -3.402823466e38f;
   int a = 0;
+  float sc[16];
 #pragma unroll
   for (int o = 0; o < 16; ++o) {
     if (o >= n_out) break;
-    const float sc = score(o);
-    if (sc > best || o == 0) { best = sc; a = o; }
+    sc[o] = score(o);
+    if (sc[o] > best || o == 0) { best = sc[o]; a = o; }
   }
   arg = a;
   if (kind == 1) {
@@ -330,7 +335,7 @@ __device__ __forceinline__ void head_readout(int kind, int n_out, int c_out, con
 #pragma unroll
   for (int o = 0; o < 16; ++o) {
     if (o >= n_out) break;
-    den += expf(score(o) - best);
+    den += expf(sc[o] - best);
   }
   conf = fminf(fmaxf(1.f / den, 0.f), 1.f);
 }
@@ -422,7 +427,9 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
     }
     mbar_init(&bars[BAR_WEIGHTS], 1);
     mbar_init(&bars[BAR_DRAIN], 1);
-    for (int r = 0; r < 4; ++r) mbar_init(&bars[BAR_FLAGS + r], 4);
+    // the flags of a tile come from the 4 half-0 stencil warps, or with the adaptive rules from
+    // all 8 (16 cells each)
+    for (int r = 0; r < 4; ++r) mbar_init(&bars[BAR_FLAGS + r], Cfg::ADAPTIVE ? 8 : 4);
     fence_mbar_init();
   }
   // Every chunk row of a window stage ends with a padding cell (index win_cells): the stencil
@@ -749,7 +756,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           i = (int)fdiv((unsigned)p, A.div_w);
           j = p - i * W;
         }
-        if (half == 0 && A.fire_mode < 2) {
+        if (!Cfg::ADAPTIVE && half == 0) {
           // per-row side information for the epilogue: bit 0 the fire decision of this step,
           // bit 1 given, bit 2 valid (the adaptive rules are evaluated after z, below)
           uint32_t fl = 0;
@@ -883,19 +890,24 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
             }
           }
         }
-        // adaptive rules in the hi/lo layout: the hi parts of the readout slice are read from the
-        // window now, before z is handed off (the epilogue releases the stage after that)
+        // Adaptive rules: every stencil warp takes 16 cells of the tile, lanes 0..15, cell ma.
+        // In the hi/lo layout the hi parts of the readout slice are read from the window now,
+        // before z is handed off (the epilogue releases the stage after that).
+        const int ma = quarter * 32 + half * 16 + (lane & 15);
+        const unsigned ga = (unsigned)t * kTileM + ma;
+        const bool va = Cfg::ADAPTIVE && lane < 16 && (long long)ga < total;
         float xhi[16];
 #pragma unroll
         for (int c = 0; c < 16; ++c) xhi[c] = 0.f;
-        if constexpr (Cfg::HILO) {
-          if (half == 0 && A.fire_mode >= 2 && valid) {
+        if constexpr (Cfg::HILO && Cfg::ADAPTIVE) {
+          if (va) {
+            const int ca = ma + W + 1;  // window index of cell ma
 #pragma unroll
             for (int c = 0; c < 16; ++c)
               if (c < A.c_out) {
                 const int cc = A.out_off + c;
                 xhi[c] = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(
-                    win + ((cc >> 3) * (WC + 1) + c0) * 16 + (cc & 7) * 2));
+                    win + ((cc >> 3) * (WC + 1) + ca) * 16 + (cc & 7) * 2));
               }
           }
         }
@@ -908,17 +920,21 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           // state) from this window and releases it
           if constexpr (!Cfg::HILO) mbar_arrive(&bars[BAR_WIN_EMPTY + stage]);
         }
-        if (half == 0 && A.fire_mode >= 2) {
+        if constexpr (Cfg::ADAPTIVE) {
           // adaptive rules: the fire decision needs the confidence of the cell's fp32 state; it
           // is evaluated after z is handed to the MMA warp (the epilogue needs it a tile later)
-          uint32_t fl = 0;
-          if (valid) {
-            const int row = A.inst_row ? A.inst_row[inst] : (int)fdiv((unsigned)inst, A.div_k);
-            const bool gv = A.given[(long long)row * A.HW + p] != 0;
-            fl = 4u | (gv ? 2u : 0u);
-            fl |= adaptive_fire<Cfg>(A, s, t, m, inst, p, gv, xhi) ? 1u : 0u;
+          if (lane < 16) {
+            uint32_t fl = 0;
+            if (va) {
+              const int inst_a = (int)fdiv(ga, A.div_hw);
+              const int p_a = (int)(ga - (unsigned)inst_a * A.HW);
+              const int row = A.inst_row ? A.inst_row[inst_a] : (int)fdiv((unsigned)inst_a, A.div_k);
+              const bool gv = A.given[(long long)row * A.HW + p_a] != 0;
+              fl = 4u | (gv ? 2u : 0u);
+              fl |= adaptive_fire<Cfg>(A, s, t, ma, inst_a, p_a, gv, xhi) ? 1u : 0u;
+            }
+            s_flags[(it & 3) * kTileM + ma] = (uint8_t)fl;
           }
-          s_flags[(it & 3) * kTileM + m] = (uint8_t)fl;
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars[BAR_FLAGS + (it & 3)]);
         }

@@ -84,3 +84,34 @@ def test_preset_100_step_rollout_agrees_with_reference(name, precision):
     solved = [bool((dec[i][~gv[i]] == tg[i][~gv[i]]).all()) for i in range(B)]
     solved_ref = [bool((ref[i][~gv[i]] == tg[i][~gv[i]]).all()) for i in range(B)]
     assert solved == solved_ref
+
+
+@pytest.mark.parametrize("name", NAMES)
+@pytest.mark.parametrize("rule", ["adaptive", "threshold"])
+def test_preset_confidence_driven_firing_matches_oracle(name, rule):
+    """The confidence-driven fire rules on the trained presets (l2 head): the continuous rule
+    p = 0.9 (1 - conf) + 0.1 and the reference's threshold rule (src/nca/model.py:566-593), in
+    split mode against the oracle's rollout with the same Philox stream: update counts exact,
+    states within the split-mode tolerance."""
+    import oracle.nca_oracle as O
+
+    g, eng, _, _, _, _ = setup(name, "split")
+    cfg = NCAConfig.from_dict(json.loads(str(g[f"{name}__config"])))
+    w = {k.split("__w__")[1]: g[k] for k in g.files if k.startswith(f"{name}__w__")}
+    p = O.params_from_arrays(w, cfg)
+    inputs, given = g[f"{name}__inputs"].astype(np.int64), g[f"{name}__given"]
+    K, D, seed = 2, 10, 5
+    n, H, W = inputs.shape
+    b = eng.batch_from_boards(inputs, given, K)
+    st = eng.new_state(n * K, H * W)
+    eng.init_state(st, b)
+    upd = torch.zeros(n * K, dtype=torch.int32, device=DEV)
+    thr = (0.1, 0.6, True) if rule == "threshold" else None
+    eng.run(st, b, D, mode=rule, p_fire=0.5, seed=seed, adaptive=(0.9, 0.1), updates=upd,
+            threshold=thr)
+    x = eng.store_nchw(st).reshape(n * K, cfg.channels, H, W).cpu().numpy()
+    eng.check()
+    ref = O.rollout(p, inputs, given, K, D, channels=cfg.channels, fire="adaptive_philox", seed=seed,
+                    p_fire=0.5, adaptive=(0.9, 0.1), threshold=thr)
+    assert np.array_equal(upd.cpu().numpy(), ref["updates"])
+    assert np.abs(x - ref["x"]).max() <= 1e-4 * np.abs(ref["x"]).max()

@@ -306,7 +306,7 @@ def run_ours(args) -> None:
             "data": "synthetic",
             "config": {"workload": bc.name, "boards": n_total, "boards_per_gpu": bc.n_boards, "k": K,
                        "depth": bc.depth,
-                       "hw": HW, "task": bc.task, "parallelism": f"boards sharded over {world} GPU(s)",
+                       "hw": HW, "task": bc.task, "parallelism": f"{bc.n_boards} boards per GPU on {world} GPU(s)",
                        "l2": f"state {st.buffer.numel() / 1e9:.1f} GB > 126 MB L2 (inputs larger than L2)"},
             "roofline": roof,
             "e2e": None if e2e_value is None else {
@@ -317,7 +317,7 @@ def run_ours(args) -> None:
         }
         if world == 1 and not args.no_cpu_baseline:
             nb, stp = cpu_sample_size(bc)
-            r_, sample = cpu_rollout_rate(bc, boards, min(nb, len(boards)), stp, os.cpu_count() or 1)
+            r_, sample = cpu_rollout_rate(bc, shard, min(nb, len(shard)), stp, os.cpu_count() or 1)
             line["cpu_baseline"] = {"value": r_, "unit": UNIT, "cores": os.cpu_count() or 1,
                                     "kind": "port", "sample": sample}
         print(json.dumps(line), flush=True)

@@ -312,7 +312,8 @@ def rollout(model, task: Task, boards: Boards, rc, seed: int = 0, task_ids=None,
         r_pred[idx] = r["pred"]
         r_conf[idx] = r["board_conf"]
         r_upd[idx] = updates.double()
-        out_pred[start : start + n] = r_pred.reshape(n, K, H, W).long().cpu().numpy()
+        # the decoded tokens cross as bytes and widen to int64 in the host array's own write
+        out_pred[start : start + n] = r_pred.reshape(n, K, H, W).cpu().numpy()
         out_conf[start : start + n] = r_conf.reshape(n, K).cpu().numpy()
         out_upd[start : start + n] = r_upd.reshape(n, K).cpu().numpy()
         out_alive[start : start + n] = r_alive.reshape(n, K).cpu().numpy()

@@ -3,15 +3,16 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfg2] [--precision bf16]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N
-    python bench.py --impl reference      # the CPU restatement of the reference, host cores
+    python bench.py --impl reference      # the reference's step loop in torch fp32, host cores
 
-One bench step = one complete rollout of the workload's boards on every rank (weak scaling:
-rank r runs its own boards as boards [r * n, (r + 1) * n) of an N-times larger job): state
-init, `depth` NCA steps for K trials per board (the persistent tcgen05 step kernel; pruning /
-adaptive firing as the workload says), readout and conf@K selection, and for N > 1 the
-all-gather of the per-board results.  Inputs are resident in HBM; e2e repeats the step through
-the public drop-in API `ncas_b200.rollout.rollout` with boards from host memory and results
-copied back.  The metric is cell-updates/s (board x trial x cell x step), whole job.
+One bench step = one complete rollout of the workload's boards, split evenly over the ranks with
+all K trials of a board on one rank (strong scaling; --scaling weak gives every rank the full
+board count instead): state init, `depth` NCA steps for K trials per board (the persistent
+tcgen05 step kernel; pruning / adaptive firing as the workload says), readout and conf@K
+selection, and for N > 1 the all-gather of the per-board results.  Inputs are resident in HBM;
+e2e repeats the step through the public drop-in API `ncas_b200.rollout.rollout` with boards from
+host memory and results copied back.  The metric is cell-updates/s (board x trial x cell x
+step), whole job.  The line also carries `split`: the same workload in the parity precision.
 """
 
 from __future__ import annotations
@@ -65,6 +66,8 @@ class ClockSampler:
         self.lines: list[str] = []
 
     def __enter__(self):
+        if self.gpu is None:
+            return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -101,36 +104,55 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------ CPU baseline
-def cpu_rollout_rate(bc, boards, n_boards: int, n_steps: int, threads: int):
-    """The oracle (numpy restatement of the reference) on a bounded sample of the workload:
-    n_boards boards x all K trials x n_steps steps.  Returns (cell-updates/s, sample str)."""
+def _host_threads() -> int:
+    """All host cores, whatever torchrun exported: torch's pool and the BLAS pools are set
+    explicitly (torchrun sets OMP_NUM_THREADS=1 for every rank)."""
+    n = os.cpu_count() or 1
+    import torch
+
+    torch.set_num_threads(n)
+    try:
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(limits=n)
+    except ImportError:
+        pass
+    return n
+
+
+def cpu_rollout_rate(bc, boards, budget_s: float = 12.0):
+    """The reference's step loop computed with torch on the host cores (oracle/torch_cpu.py:
+    F.conv2d perception, 1x1-conv MLP, torch.rand fire draws, fp32), on a bounded sample of the
+    workload: a few boards x all K trials x enough steps for about `budget_s` seconds.
+    Returns (cell-updates/s, sample description, threads)."""
     import oracle.nca_oracle as O
+    import oracle.torch_cpu as TC
     from ncas_b200.configs import model_config, synthetic_params
 
-    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    threads = _host_threads()
     cfg = model_config(bc.task)
-    p = O.params_from_arrays(synthetic_params(cfg, 0), cfg)
+    m = TC.TorchCpuNca(O.params_from_arrays(synthetic_params(cfg, 0), cfg), cfg.channels)
+    adaptive = (0.9, 0.1) if bc.adaptive else None
+    # a few boards: about 50k-100k cells per step, like the reference's own per-pass batches
+    n_boards = max(1, min(len(boards), 100_000 // (bc.k * bc.hw)))
     sub = boards.subset(np.arange(n_boards))
-    fire = "adaptive_philox" if bc.adaptive else "philox"
-    O.rollout(p, sub.inputs[:1], sub.given[:1], bc.k, 1, channels=cfg.channels, fire=fire, seed=0)  # warm-up
+    TC.rollout_steps(m, sub.inputs, sub.given, bc.k, 1, bc.p_fire, adaptive)  # warm-up
     t0 = time.perf_counter()
-    O.rollout(p, sub.inputs, sub.given, bc.k, n_steps, channels=cfg.channels, fire=fire, seed=0)
+    TC.rollout_steps(m, sub.inputs, sub.given, bc.k, 2, bc.p_fire, adaptive)
+    per_step = (time.perf_counter() - t0) / 2
+    steps = max(2, min(bc.depth, int(budget_s / max(per_step, 1e-6))))
+    t0 = time.perf_counter()
+    TC.rollout_steps(m, sub.inputs, sub.given, bc.k, steps, bc.p_fire, adaptive)
     dt = time.perf_counter() - t0
-    cu = n_boards * bc.k * bc.hw * n_steps
-    return cu / dt, f"{n_boards} boards x K={bc.k} x {n_steps} steps ({cu} cell-updates, {dt:.1f} s)"
-
-
-def cpu_sample_size(bc) -> tuple[int, int]:
-    """A sample of roughly 10-20 s of oracle work on a few host cores."""
-    per_cu = {"maze": 8.0e-6, "sudoku": 6.0e-6}[bc.task]  # seconds per cell-update on 8 cores, rough
-    target = 12.0
-    n_boards = max(1, min(bc.n_boards, int(target / (per_cu * bc.k * bc.hw * 8)) or 1))
-    steps = max(1, min(bc.depth, int(target / (per_cu * n_boards * bc.k * bc.hw))))
-    return n_boards, steps
+    cu = n_boards * bc.k * bc.hw * steps
+    sample = (f"{n_boards} boards x K={bc.k} x {steps} steps of {bc.name} ({cu} cell-updates, "
+              f"{dt:.1f} s, torch fp32 on {threads} threads)")
+    return cu / dt, sample, threads
 
 
 def run_reference(args) -> None:
-    """--impl reference: the reference's algorithm (CPU restatement) on the host cores."""
+    """--impl reference: the reference's step loop as the reference computes it (torch fp32
+    operators on the host cores), rank 0 only."""
     from ncas_b200.configs import CONFIGS, boards_for
 
     rank = int(os.environ.get("RANK", "0"))
@@ -138,21 +160,18 @@ def run_reference(args) -> None:
         return
     bc = CONFIGS[args.workload]
     boards = boards_for(bc, seed=0, n=min(bc.n_boards, 64))
-    threads = os.cpu_count() or 1
-    n_boards, steps = cpu_sample_size(bc)
-    n_boards = min(n_boards, len(boards))
     for _ in range(args.warmup):
-        cpu_rollout_rate(bc, boards, n_boards, max(1, steps // 4), threads)
+        cpu_rollout_rate(bc, boards, budget_s=1.0)
     rates = []
-    sample = ""
+    sample, threads = "", 1
     for _ in range(args.steps):
-        r, sample = cpu_rollout_rate(bc, boards, n_boards, steps, threads)
+        r, sample, threads = cpu_rollout_rate(bc, boards, budget_s=4.0)
         rates.append(r)
     value = float(np.median(rates))
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": n_boards * bc.k * bc.hw * steps / value * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": bc.cell_updates / value * 1e3,
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": {"workload": bc.name, "boards": bc.n_boards, "k": bc.k,
                                         "depth": bc.depth, "hw": bc.hw},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
@@ -162,12 +181,45 @@ def run_reference(args) -> None:
 
 
 # --------------------------------------------------------------------------------- GPU arm
+def roofline(bc, precision: str, kdur_ms: list[float], cells: list[int]) -> dict:
+    """The step kernel's roofline from its CUDA-event launch times: the lower of the tensor
+    ceiling (GEMM FLOPs) and the HBM ceiling (algorithmic bytes) per cell-update."""
+    pk, pk_kind = peaks()
+    flop_per_cu = bc.flop_per_cell_update
+    # split mode runs every GEMM on the hi and the lo part of its activations: twice the MMAs
+    executed = flop_per_cu * (2 if precision == "split" else 1)
+    avg_kms = float(np.mean(kdur_ms))
+    avg_cells = float(np.mean(cells))
+    bytes_per_cu = bc.bytes_per_cell_update(precision)
+    tb = profile_traffic(bc.name) if precision == "bf16" else None
+    t_peak = pk.get("bf16_tflops_sustained", 1400.0)
+    t_burst = pk.get("bf16_tflops", 1590.0)
+    h_peak = pk.get("hbm_gbs", 6650.0)
+    t_ach = flop_per_cu * avg_cells / (avg_kms / 1e3) / 1e12
+    t_frac = t_ach / t_peak
+    h_frac = bytes_per_cu * avg_cells / (avg_kms / 1e3) / 1e9 / h_peak
+    if t_peak * 1e12 / executed <= h_peak * 1e9 / bytes_per_cu:
+        roof = {"bound": "tensor", "achieved": t_ach, "peak": t_peak, "unit": "TFLOP/s",
+                "frac": t_frac, "peak_kind": f"{pk_kind} bf16 sustained",
+                "frac_of_burst": t_ach / t_burst, "other": {"bound": "hbm", "frac": h_frac}}
+    else:
+        roof = {"bound": "hbm", "achieved": h_frac * h_peak, "peak": h_peak, "unit": "GB/s",
+                "frac": h_frac, "peak_kind": f"{pk_kind} copy bandwidth",
+                "other": {"bound": "tensor", "frac": t_frac}}
+    if precision == "split":
+        roof["executed_tflops"] = executed * avg_cells / (avg_kms / 1e3) / 1e12
+    roof.update({"traffic": None if tb is None else tb * avg_cells, "kernel": "nca_step_kernel",
+                 "flop_per_cell_update": flop_per_cu, "bytes_per_cell_update": bytes_per_cu,
+                 "kernel_ms": avg_kms})
+    return roof
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
 
     from ncas_b200.configs import CONFIGS, boards_for, build, task_for
-    from ncas_b200.distributed import gather_results
+    from ncas_b200.distributed import gather_results, shard_range
     from ncas_b200.rollout import RolloutConfig, rollout
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -187,73 +239,88 @@ def run_ours(args) -> None:
         import dataclasses
 
         bc = dataclasses.replace(bc, n_boards=args.boards or bc.n_boards, depth=args.depth or bc.depth)
-    model = build(bc.task, seed=0, device=dev, precision=args.precision)
-    eng = model.engine()
-    # Weak scaling: every rank runs the workload's full board count on boards of its own (seed =
-    # rank; rank 0's are the one-GPU boards), as global boards [rank * n, (rank + 1) * n) of an
-    # N-times larger job, so the Philox streams of all ranks are distinct.
-    n_total = bc.n_boards * world
-    s = rank * bc.n_boards
-    shard = boards_for(bc, seed=rank)
+    # Strong scaling (default): the workload's boards are split evenly over the ranks, all K
+    # trials of a board on one rank, as one job.  Weak scaling: every rank runs the workload's
+    # board count on boards of its own (global boards [rank * n, (rank + 1) * n) of an N-times
+    # larger job).  A workload with fewer boards than ranks (cfg1) runs replicas (weak).
+    scaling = args.scaling if bc.n_boards >= world else "weak"
+    if scaling == "strong":
+        n_total = bc.n_boards
+        s, e = shard_range(n_total, world, rank)
+        shard = boards_for(bc, seed=0).subset(np.arange(s, e))
+    else:
+        n_total = bc.n_boards * world
+        s = rank * bc.n_boards
+        shard = boards_for(bc, seed=rank)
     n, K, HW = len(shard), bc.k, bc.hw
-    batch = eng.batch_from_boards(shard.inputs, shard.given, K, inst_offset=s * K)
-    st = eng.new_state(n * K, HW)
-    updates = torch.zeros(n * K, dtype=torch.int32, device=dev)
+    total_cu = n_total * K * HW * bc.depth  # all ranks' cell-updates of one bench step
     adaptive = (0.9, 0.1) if bc.adaptive else None
     segs = list(range(0, bc.depth, bc.prune_every)) + [bc.depth] if bc.prune_every else [0, bc.depth]
-    kern_ms: list[float] = []
-    kern_cells: list[int] = []
-
-    def one_step(timed: bool):
-        eng.init_state(st, batch)
-        for a, b in zip(segs[:-1], segs[1:]):
-            ev0 = torch.cuda.Event(enable_timing=True)
-            ev1 = torch.cuda.Event(enable_timing=True)
-            ev0.record()
-            eng.run(st, batch, b - a, mode="adaptive" if adaptive else "philox", p_fire=bc.p_fire,
-                    seed=0, step0=a, updates=updates, adaptive=adaptive or (0.9, 0.1))
-            ev1.record()
-            if timed:
-                kern_ms.append((ev0, ev1))
-                kern_cells.append(n * K * HW * (b - a))
-            if b < bc.depth:
-                r = eng.readout(st, batch)
-                eng.prune_refill(st, r["pred"], r["board_conf"], n, K, bc.n_cap)
-        r = eng.readout(st, batch)
-        idx, best, bp = eng.select(r["board_conf"], n, K, pred=r["pred"], hw=HW)
-        if world > 1:
-            gather_results(best, idx, bp, n_total)
-        return best
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    for _ in range(args.warmup):
-        one_step(False)
-    eng.check()
-    barrier()
-    l0 = eng.launches
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    def max_over_ranks(v: float) -> float:
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def measure(precision: str, steps: int, warmup: int, clocks: bool):
+        """`warmup` then `steps` timed bench steps of the workload in `precision`: returns
+        (ms of the timed region (max over ranks), step-kernel event pairs, their cell-updates,
+        library launches, clock summary, state bytes)."""
+        model = build(bc.task, seed=0, device=dev, precision=precision)
+        eng = model.engine()
+        batch = eng.batch_from_boards(shard.inputs, shard.given, K, inst_offset=s * K)
+        st = eng.new_state(n * K, HW)
+        updates = torch.zeros(n * K, dtype=torch.int32, device=dev)
+        kern, kern_cells = [], []
+
+        def one_step(timed: bool):
+            eng.init_state(st, batch)
+            for a, b in zip(segs[:-1], segs[1:]):
+                ev0 = torch.cuda.Event(enable_timing=True)
+                ev1 = torch.cuda.Event(enable_timing=True)
+                ev0.record()
+                eng.run(st, batch, b - a, mode="adaptive" if adaptive else "philox", p_fire=bc.p_fire,
+                        seed=0, step0=a, updates=updates, adaptive=adaptive or (0.9, 0.1))
+                ev1.record()
+                if timed:
+                    kern.append((ev0, ev1))
+                    kern_cells.append(n * K * HW * (b - a))
+                if b < bc.depth:
+                    r = eng.readout(st, batch)
+                    eng.prune_refill(st, r["pred"], r["board_conf"], n, K, bc.n_cap)
+            r = eng.readout(st, batch)
+            idx, best, bp = eng.select(r["board_conf"], n, K, pred=r["pred"], hw=HW)
+            if world > 1:
+                gather_results(best, idx, bp, n_total)
+
+        for _ in range(warmup):
+            one_step(False)
+        eng.check()
         barrier()
-        t0.record()
-        for _ in range(args.steps):
-            one_step(True)
-        t1.record()
-        barrier()
-    eng.check()
-    launches = eng.launches - l0
-    ms = t0.elapsed_time(t1)
-    kdur = [a.elapsed_time(b) for a, b in kern_ms]
-    t_max = torch.tensor([ms], device=dev)
-    if world > 1:
-        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
-    ms = float(t_max.item())
-    total_cu = bc.cell_updates * world * args.steps  # all ranks' boards
-    value = total_cu / (ms / 1e3)
+        l0 = eng.launches
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local if clocks else None) as clk:
+            barrier()
+            t0.record()
+            for _ in range(steps):
+                one_step(True)
+            t1.record()
+            barrier()
+        eng.check()
+        ms = max_over_ranks(t0.elapsed_time(t1))
+        kdur = [a.elapsed_time(b) for a, b in kern]
+        return ms, kdur, kern_cells, eng.launches - l0, clk.summary(), st.buffer.numel(), model
+
+    ms, kdur, kcells, launches, clocks, state_bytes, model = measure(args.precision, args.steps,
+                                                                     args.warmup, True)
+    value = total_cu * args.steps / (ms / 1e3)
 
     # ---- e2e through the public API (host boards in, host results out)
     e2e_value, h2d, d2h = None, 0, 0
@@ -270,56 +337,45 @@ def run_ours(args) -> None:
         for _ in range(e2e_steps):
             res = rollout(model, task, shard, rc, seed=0, board_offset=s)
         barrier()
-        e2e_s = torch.tensor([time.perf_counter() - w0], device=dev)
+        e2e_s = max_over_ranks(time.perf_counter() - w0)
+        e2e_value = total_cu * e2e_steps / e2e_s
+        io = torch.tensor([shard.inputs.nbytes + shard.given.nbytes + shard.targets.nbytes,
+                           res.pred.size + res.conf.nbytes + res.cell_updates.nbytes],
+                          dtype=torch.int64, device=dev)
         if world > 1:
-            dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
-        e2e_value = bc.cell_updates * world * e2e_steps / float(e2e_s.item())
-        h2d = int(shard.inputs.nbytes + shard.given.nbytes + shard.targets.nbytes)
-        d2h = int(res.pred.size + res.conf.nbytes + res.cell_updates.nbytes)
+            dist.all_reduce(io)
+        h2d, d2h = int(io[0]), int(io[1])
+
+    # ---- the parity mode (fp32 stencil, GEMMs on bf16 hi + lo parts) on the same workload
+    split = None
+    if args.precision == "bf16" and not args.no_split:
+        sms, skdur, skcells, _, _, _, _ = measure("split", max(1, min(args.steps, 3)), 1, False)
+        split = {"value": total_cu * max(1, min(args.steps, 3)) / (sms / 1e3),
+                 "ms_per_step": sms / max(1, min(args.steps, 3)),
+                 "roofline": roofline(bc, "split", skdur, skcells)}
 
     if rank == 0:
-        pk, pk_kind = peaks()
-        flop_per_cu = bc.flop_per_cell_update
-        avg_kms = float(np.mean(kdur))
-        avg_cells = float(np.mean(kern_cells))
-        bytes_per_cu = bc.bytes_per_cell_update(args.precision)
-        tb = profile_traffic(bc.name)
-        # the roofline of the step kernel is the lower of its two ceilings (cell-updates/s)
-        t_peak = pk.get("bf16_tflops_sustained", 1400.0)
-        h_peak = pk.get("hbm_gbs", 6650.0)
-        t_frac = flop_per_cu * avg_cells / (avg_kms / 1e3) / 1e12 / t_peak
-        h_frac = bytes_per_cu * avg_cells / (avg_kms / 1e3) / 1e9 / h_peak
-        if t_peak * 1e12 / flop_per_cu <= h_peak * 1e9 / bytes_per_cu:
-            roof = {"bound": "tensor", "achieved": t_frac * t_peak, "peak": t_peak,
-                    "unit": "TFLOP/s", "frac": t_frac, "peak_kind": f"{pk_kind} bf16 sustained",
-                    "other": {"bound": "hbm", "frac": h_frac}}
-        else:
-            roof = {"bound": "hbm", "achieved": h_frac * h_peak, "peak": h_peak, "unit": "GB/s",
-                    "frac": h_frac, "peak_kind": f"{pk_kind} copy bandwidth",
-                    "other": {"bound": "tensor", "frac": t_frac}}
-        roof.update({"traffic": None if tb is None else tb * avg_cells, "kernel": "nca_step_kernel",
-                     "flop_per_cell_update": flop_per_cu, "bytes_per_cell_update": bytes_per_cu})
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if args.precision == "bf16" else "bf16x2",
+            "scaling": scaling, "vs_baseline": None, "dtype": "bf16" if args.precision == "bf16" else "bf16x2",
             "data": "synthetic",
-            "config": {"workload": bc.name, "boards": n_total, "boards_per_gpu": bc.n_boards, "k": K,
-                       "depth": bc.depth,
-                       "hw": HW, "task": bc.task, "parallelism": f"{bc.n_boards} boards per GPU on {world} GPU(s)",
-                       "l2": f"state {st.buffer.numel() / 1e9:.1f} GB > 126 MB L2 (inputs larger than L2)"},
-            "roofline": roof,
+            "config": {"workload": bc.name, "boards": n_total, "boards_per_gpu": n, "k": K,
+                       "depth": bc.depth, "hw": HW, "task": bc.task, "precision": args.precision,
+                       "parallelism": f"{n_total} boards over {world} GPU(s), all K trials of a board on one GPU",
+                       "l2": f"state {state_bytes / 1e9:.2f} GB per GPU vs 126 MB L2"},
+            "roofline": roofline(bc, args.precision, kdur, kcells),
             "e2e": None if e2e_value is None else {
-                "value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d * world,
-                "d2h_bytes_per_step": d2h * world},
+                "value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
-            "clocks": clk.summary(),
+            "clocks": clocks,
         }
+        if split is not None:
+            line["split"] = split
         if world == 1 and not args.no_cpu_baseline:
-            nb, stp = cpu_sample_size(bc)
-            r_, sample = cpu_rollout_rate(bc, shard, min(nb, len(shard)), stp, os.cpu_count() or 1)
-            line["cpu_baseline"] = {"value": r_, "unit": UNIT, "cores": os.cpu_count() or 1,
-                                    "kind": "port", "sample": sample}
+            r_, sample, threads = cpu_rollout_rate(bc, shard)
+            line["cpu_baseline"] = {"value": r_, "unit": UNIT, "cores": threads, "kind": "port",
+                                    "sample": sample}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -335,6 +391,9 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the public-API (host buffers) pass")
+    ap.add_argument("--no-split", action="store_true", help="skip the split-precision measurement")
+    ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
+                    help="strong: the workload's boards split over the GPUs; weak: every GPU runs them")
     ap.add_argument("--boards", type=int, default=None, help="smaller case of the workload (profiling)")
     ap.add_argument("--depth", type=int, default=None, help="smaller case of the workload (profiling)")
     args = ap.parse_args()

@@ -264,24 +264,27 @@ int32_t nca_b200_selftest_timeout(int32_t* ctrl, int32_t timeout_ms, void* strea
  * GPU that loads the library holds it until the process exits. */
 #define NCA_B200_STATIC_SCRATCH_BYTES (16u << 20)
 
-/* For callers that cannot allocate device memory: code running inside a CUDA graph being built,
- * a host framework whose allocator owns all device memory and hands out only the caller's
- * tensors, or an embedded runtime with a fixed memory budget.  It runs the same n_steps as
- * nca_b200_run_steps, but the kernel's scratch (the ping-pong state workspace and the four
- * control words) lives in a static 16 MiB device array inside the library instead of buffers
- * the caller allocates; the caller passes only inputs and outputs: the fp32 NCHW state before
- * (x_in) and after (x_out) the steps, both n_inst x channels x H x W.
+/* For callers that cannot allocate device memory: a host framework whose allocator owns all
+ * device memory and hands out only the caller's tensors, or an embedded runtime with a fixed
+ * device-memory budget fixed at start-up.  It runs the same n_steps as nca_b200_run_steps, but
+ * the kernel's scratch (the ping-pong state workspace and the four control words) lives in a
+ * static 16 MiB device array inside the library instead of buffers the caller allocates; the
+ * caller passes only inputs and outputs: the fp32 NCHW state before (x_in) and after (x_out) the
+ * steps, both n_inst x channels x H x W.
  *  - Limit: nca_b200_state_bytes(n_inst, H*W, channels, state_precision) + 256 bytes must fit in
  *    NCA_B200_STATIC_SCRATCH_BYTES, else NCA_ERR_SCRATCH (e.g. 32,000 Sudoku cells at C = 64 or one
  *    201 x 201 maze at C = 32 in bf16 mode).
  *  - It calls no allocator.  Its first call on a device looks up the device address of the array
- *    (cudaGetSymbolAddress with that device current); make that first call before any stream
- *    capture on the device.
+ *    (cudaGetSymbolAddress with that device current) and keeps it for the process; make that
+ *    first call before any stream capture on the device.  Two host threads making a first call
+ *    on one device at the same time both look the address up and store the same value.  After a
+ *    cudaDeviceReset the kept address may be stale: do not use this entry point after a reset.
  *  - All calls share the one array, which keeps the last call's contents; the call clears the
  *    control words and rewrites the state workspace before use.  Calls that overlap on the GPU
  *    (other streams, other host threads) race on the array: serialise them.
  *  - It waits for its own work: the stream is synchronised before it returns, so that a kernel
- *    timeout comes back as NCA_ERR_TIMEOUT.
+ *    timeout comes back as NCA_ERR_TIMEOUT.  It returns the status code only: the failing site
+ *    that nca_b200_ctrl_status reports through `detail` is not available here.
  * There is no counterpart in the reference: it is an addition of this library. */
 int32_t nca_b200_run_steps_static(const NcaModelDesc* m, const NcaBatchDesc* b,
                                   int32_t state_precision, const float* x_in, float* x_out,

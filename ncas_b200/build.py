@@ -14,10 +14,15 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 CSRC = ROOT / "csrc"
 OUT = ROOT / "_lib" / "libnca_b200.so"
-SOURCES = [CSRC / "api.cu"]
-DEPS = SOURCES + [CSRC / "ptx.cuh", CSRC / "step_kernel.cuh", ROOT.parent / "include" / "nca_b200.h"]
+# api.cu holds the entry points and small kernels; each steps_<C>_<HD>.cu the step-kernel
+# instances of one model shape (compiled in parallel, then linked into one library)
+SOURCES = [CSRC / "api.cu", CSRC / "steps_64_256.cu", CSRC / "steps_32_128.cu",
+           CSRC / "steps_16_128.cu", CSRC / "steps_32_256.cu"]
+HEADERS = [CSRC / "ptx.cuh", CSRC / "step_kernel.cuh", CSRC / "launch.cuh",
+           ROOT.parent / "include" / "nca_b200.h"]
+DEPS = SOURCES + HEADERS
 
-NVCC_FLAGS = [
+ARCH_FLAGS = [
     "-gencode",
     "arch=compute_100a,code=sm_100a",
     "-lineinfo",
@@ -25,8 +30,8 @@ NVCC_FLAGS = [
     "-std=c++17",
     "-Xcompiler",
     "-fPIC",
-    "-shared",
 ]
+NVCC_FLAGS = ARCH_FLAGS + ["-shared"]  # the flags of a one-step build (kept for reference)
 
 
 def nvcc() -> str:
@@ -44,19 +49,33 @@ def up_to_date() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
-    """Compile the CUDA sources into ncas_b200/_lib/libnca_b200.so (skipped when up to date)."""
+    """Compile the CUDA sources into ncas_b200/_lib/libnca_b200.so (skipped when up to date):
+    every translation unit to an object in parallel, then one shared-library link."""
     if not force and up_to_date():
         return OUT
     OUT.parent.mkdir(parents=True, exist_ok=True)
+    objdir = ROOT / "_lib" / "obj"
+    objdir.mkdir(parents=True, exist_ok=True)
+    extra = ["-Xptxas=-v"] if verbose else []
+    procs = []
+    for src in SOURCES:
+        obj = objdir / (src.stem + ".o")
+        cmd = [nvcc(), *ARCH_FLAGS, *extra, "-c", "-o", str(obj), str(src)]
+        procs.append((cmd, obj, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE,
+                                                 text=True)))
+    objs = []
+    for cmd, obj, p in procs:
+        out, err = p.communicate()
+        if p.returncode != 0:
+            raise RuntimeError(f"nvcc failed ({' '.join(cmd)}):\n{out}\n{err}")
+        if verbose:
+            print(out, err, file=sys.stderr)
+        objs.append(str(obj))
     tmp = OUT.with_suffix(".so.tmp")
-    cmd = [nvcc(), *NVCC_FLAGS, "-o", str(tmp), *map(str, SOURCES)]
-    if verbose:
-        cmd.insert(1, "-Xptxas=-v")
+    cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", str(tmp), *objs]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({' '.join(cmd)}):\n{res.stdout}\n{res.stderr}")
-    if verbose:
-        print(res.stdout, res.stderr, file=sys.stderr)
+        raise RuntimeError(f"nvcc link failed ({' '.join(cmd)}):\n{res.stdout}\n{res.stderr}")
     tmp.replace(OUT)
     return OUT
 

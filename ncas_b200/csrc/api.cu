@@ -5,14 +5,15 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <atomic>
+
 #include "../../include/nca_b200.h"
+#include "launch.cuh"
 #include "step_kernel.cuh"
 
 using namespace nca;
 
 namespace {
-
-constexpr int kMaxSmem = 232448;  // opt-in dynamic shared memory per CTA on sm_100
 
 inline int32_t cuda_status(cudaError_t e) { return e == cudaSuccess ? NCA_OK : NCA_ERR_CUDA; }
 
@@ -237,7 +238,16 @@ __global__ void readout_kernel(const float* master, const uint16_t* mirror, NcaB
   }
 }
 
-// One warp per board: first index of the maximum of (alive ? conf : -inf) over k < k_limit.
+// Order of np.argmax over (alive ? conf : -inf): a NaN is larger than every number (argmax
+// returns the first NaN), ties go to the smaller index.
+__device__ __forceinline__ bool select_better(float v, int k, float bv, int bi) {
+  const bool vn = v != v, bn = bv != bv;
+  if (vn || bn) return vn && (!bn || k < bi);
+  return v > bv || (v == bv && k < bi);
+}
+
+// One warp per board: first index of the maximum of (alive ? conf : -inf) over k < k_limit,
+// with the NaN rule of np.argmax (src/nca/rollout.py:331-332).
 __global__ void select_kernel(const float* conf, const uint8_t* alive, int n_boards, int K,
                               int k_limit, int* best_idx, float* best_conf, const uint8_t* pred,
                               int hw, uint8_t* best_pred) {
@@ -249,12 +259,12 @@ __global__ void select_kernel(const float* conf, const uint8_t* alive, int n_boa
   for (int k = lane; k < k_limit; k += 32) {
     const long long i = (long long)warp * K + k;
     const float v = (alive == nullptr || alive[i]) ? conf[i] : -INFINITY;
-    if (v > bv || (v == bv && k < bi)) { bv = v; bi = k; }
+    if (select_better(v, k, bv, bi)) { bv = v; bi = k; }
   }
   for (int o = 16; o; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
     const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    if (select_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
   }
   if (bi == 0x7fffffff) bi = 0;
   if (lane == 0) {
@@ -476,118 +486,6 @@ __global__ void selftest_wait_kernel(int* ctrl, unsigned long long timeout_ns) {
   __syncthreads();
 }
 
-template <class Cfg>
-int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaState* st, int32_t n_steps,
-                     const NcaFireDesc* fire, int32_t* ctrl, int32_t timeout_ms,
-                     cudaStream_t stream) {
-  StepArgs A;
-  memset(&A, 0, sizeof(A));
-  A.n_inst = b->n_inst;
-  A.H = b->height;
-  A.W = b->width;
-  A.HW = b->height * b->width;
-  A.K = b->trials;
-  A.div_hw = make_fastdiv((unsigned)A.HW);
-  A.div_w = make_fastdiv((unsigned)A.W);
-  A.div_k = make_fastdiv((unsigned)A.K);
-  A.total = (long long)b->n_inst * A.HW;
-  if (A.total + 2 * kTileM + 2LL * A.W >= (1LL << 31)) return NCA_ERR_UNSUPPORTED;  // 32-bit cell ids
-  A.n_tiles = st->n_tiles;
-  A.inst_offset = b->inst_offset;
-  A.n_steps = n_steps;
-  A.step0 = fire->step0;
-  A.win_cells = kTileM + 2 * b->width + 2;
-  A.c_in = m->c_in;
-  A.in_off = m->in_offset;
-  A.c_out = m->c_out;
-  A.out_off = m->out_offset;
-  A.n_out = m->n_out;
-  A.fixed_taps = m->fixed_taps;
-  memcpy(A.taps, m->taps, sizeof(A.taps));
-  memcpy(A.head_w, m->head_w, sizeof(A.head_w));
-  memcpy(A.head_b, m->head_b, sizeof(A.head_b));
-  A.wimg = reinterpret_cast<const uint8_t*>(m->weights);
-  A.wimg_lo = (st->precision == NCA_PREC_SPLIT) ? reinterpret_cast<const uint8_t*>(m->weights_lo) : nullptr;
-  A.head_kind = m->head_kind;
-  memcpy(A.pad, m->pad, sizeof(A.pad));
-  A.b1 = m->b1;
-  A.b2 = m->b2;
-  A.given = b->given;
-  A.clamp = b->clamp;
-  A.inst_row = b->inst_row;
-  A.inst_id = b->inst_id;
-  A.master[0] = st->master[0];
-  A.master[1] = st->master[1];
-  A.mirror[0] = st->mirror[0];
-  A.mirror[1] = st->mirror[1];
-  A.cur = st->cur;
-  A.fire_mode = fire->mode;
-  A.p_fire = fire->p_fire;
-  A.ad_scale = fire->adapt_scale;
-  A.ad_bias = fire->adapt_bias;
-  A.p_low = fire->p_low;
-  A.tau = fire->tau;
-  A.given_confident = fire->given_confident;
-  A.seed = fire->seed;
-  A.masks = fire->masks;
-  A.uniforms = fire->uniforms;
-  A.updates = fire->updates;
-  A.noise_mode = fire->noise_mode;
-  A.noise_p_t = fire->noise_p_t;
-  A.noise_p_s = fire->noise_p_s;
-  A.noise_sigma = fire->noise_sigma;
-  A.noise_until = fire->noise_until;
-  A.noise = fire->noise;
-  A.ctrl = ctrl;
-  A.timeout_ns = (unsigned long long)(timeout_ms > 0 ? timeout_ms : 10000) * 1000000ull;
-
-  // Window stages: in the hi/lo layout a window lives from the stencil to the epilogue (which
-  // reads the hi part of the old state from it), so more stages keep the stencil ahead.
-  int stages = Cfg::HILO ? kMaxStages : 2;
-  int smem = SmemLayout<Cfg>(stages, A.win_cells, A.wimg_lo != nullptr).total + 1024;
-  while (smem > kMaxSmem && stages > 1) {
-    --stages;
-    smem = SmemLayout<Cfg>(stages, A.win_cells, A.wimg_lo != nullptr).total + 1024;
-  }
-  if (smem > kMaxSmem) return NCA_ERR_UNSUPPORTED;
-  A.stages = stages;
-
-  int dev = 0, sms = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return NCA_ERR_CUDA;
-  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (e != cudaSuccess) return NCA_ERR_CUDA;
-  const long long grid_ll = A.n_tiles < sms ? A.n_tiles : sms;
-  const int grid = (int)(grid_ll > 0 ? grid_ll : 1);
-  // Steps are ordered by per-tile step counters when every CTA has few tiles (a grid barrier
-  // would idle the whole GPU at each step boundary), else by the grid barrier on ctrl[2], whose
-  // cost is then small against the step (the per-tile form costs the epilogue registers and the
-  // MMA warp a publisher lane).
-  const bool tiledep = n_steps > 1 && A.n_tiles <= (long long)kTileDepPerCta * grid;
-  using CfgTD = StepCfg<Cfg::C, Cfg::HD, Cfg::SPLIT, Cfg::NOISE, true, Cfg::ADAPTIVE>;
-  auto kern = tiledep ? nca_step_kernel<CfgTD> : nca_step_kernel<Cfg>;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return NCA_ERR_CUDA;
-  A.tile_steps = tiledep ? st->tile_steps : nullptr;
-  if (tiledep) {
-    e = cudaMemsetAsync(st->tile_steps, 0, (size_t)st->n_tiles * sizeof(uint32_t), stream);
-    if (e != cudaSuccess) return NCA_ERR_CUDA;
-  }
-  e = cudaMemsetAsync(ctrl + 2, 0, sizeof(int32_t), stream);
-  if (e != cudaSuccess) return NCA_ERR_CUDA;
-  if (n_steps > 1) {
-    void* args[] = {&A};
-    e = cudaLaunchCooperativeKernel((const void*)kern, dim3(grid), dim3(kThreads), args,
-                                    (size_t)smem, stream);
-  } else {
-    kern<<<grid, kThreads, smem, stream>>>(A);
-    e = cudaGetLastError();
-  }
-  if (e != cudaSuccess) return NCA_ERR_CUDA;
-  st->cur = (st->cur + n_steps) & 1;
-  return NCA_OK;
-}
-
 bool model_ok(const NcaModelDesc* m) {
   if (!m || !m->weights || !m->b1 || !m->b2) return false;
   if (m->perception != 4 * m->channels) return false;
@@ -640,7 +538,7 @@ int32_t nca_b200_device_info(int32_t device, int32_t* sm_count, int32_t* cc_majo
   if (cc_minor) *cc_minor = mi;
   if (ma != 10) return NCA_ERR_DEVICE;
   cudaFuncAttributes fa;
-  if (cudaFuncGetAttributes(&fa, nca_step_kernel<StepCfg<64, 256, false>>) != cudaSuccess)
+  if (step_kernel_attributes(&fa) != cudaSuccess)
     return NCA_ERR_DEVICE;
   return NCA_OK;
 }
@@ -762,26 +660,12 @@ int32_t nca_b200_run_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaStat
   const bool noise = fire->noise_mode != NCA_NOISE_NONE;
   const bool adaptive = fire->mode >= NCA_FIRE_ADAPTIVE_PHILOX;  // fire decisions on the confidence
   auto launch = [&](int32_t n, const NcaFireDesc* f) -> int32_t {
-#define NCA_LAUNCH_AD(CC, HH, SP, NZ)                                                             \
-  return adaptive ? launch_steps<StepCfg<CC, HH, SP, NZ, false, true>>(m, b, st, n, f, ctrl, timeout_ms, s) \
-                  : launch_steps<StepCfg<CC, HH, SP, NZ>>(m, b, st, n, f, ctrl, timeout_ms, s);
-#define NCA_LAUNCH(CC, HH)                                                                        \
-  if (C == CC && HD == HH) {                                                                      \
-    if (noise) {                                                                                  \
-      if (split) { NCA_LAUNCH_AD(CC, HH, true, true) }                                            \
-      NCA_LAUNCH_AD(CC, HH, false, true)                                                          \
-    }                                                                                             \
-    if (split) { NCA_LAUNCH_AD(CC, HH, true, false) }                                             \
-    NCA_LAUNCH_AD(CC, HH, false, false)                                                           \
-  }
     // the benchmark models (32, 128), (64, 256) and the reference's maze presets (16, 128),
     // (32, 256) (maze_ood, maze_hard: src/nca/model.py:656-700)
-    NCA_LAUNCH(32, 128)
-    NCA_LAUNCH(64, 256)
-    NCA_LAUNCH(16, 128)
-    NCA_LAUNCH(32, 256)
-#undef NCA_LAUNCH
-#undef NCA_LAUNCH_AD
+    if (C == 32 && HD == 128) return launch_shape_32_128(split, noise, adaptive, m, b, st, n, f, ctrl, timeout_ms, s);
+    if (C == 64 && HD == 256) return launch_shape_64_256(split, noise, adaptive, m, b, st, n, f, ctrl, timeout_ms, s);
+    if (C == 16 && HD == 128) return launch_shape_16_128(split, noise, adaptive, m, b, st, n, f, ctrl, timeout_ms, s);
+    if (C == 32 && HD == 256) return launch_shape_32_256(split, noise, adaptive, m, b, st, n, f, ctrl, timeout_ms, s);
     return NCA_ERR_UNSUPPORTED;
   };
   if (st->clamped) return launch(n_steps, fire);
@@ -958,19 +842,23 @@ namespace {
 __device__ __align__(256) uint8_t g_static_scratch[NCA_B200_STATIC_SCRATCH_BYTES];
 
 constexpr int kMaxDevices = 64;
-void* g_static_scratch_addr[kMaxDevices] = {};
+// Per device, the address of g_static_scratch, looked up on the first call with the device
+// current.  Atomic: host threads that make a first call together each look it up and store the
+// same value.  A cudaDeviceReset can move the module, so the kept address is valid only until a
+// reset (documented in the header).
+std::atomic<void*> g_static_scratch_addr[kMaxDevices];
 
 // Device address of g_static_scratch on the current device (looked up once per device).
 int32_t static_scratch(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return NCA_ERR_DEVICE;
-  if (g_static_scratch_addr[dev] == nullptr) {
-    void* p = nullptr;
+  void* p = g_static_scratch_addr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
     if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || p == nullptr)
       return NCA_ERR_CUDA;
-    g_static_scratch_addr[dev] = p;
+    g_static_scratch_addr[dev].store(p, std::memory_order_release);
   }
-  *out = g_static_scratch_addr[dev];
+  *out = p;
   return NCA_OK;
 }
 

@@ -25,7 +25,8 @@ def pack_results(best_conf: torch.Tensor, best_idx: torch.Tensor, answers: torch
     """(n,) fp32, (n,) int32, (n, hw) uint8 -> (n, 8 + hw) uint8 rows."""
     n = best_conf.shape[0]
     head = torch.stack([best_conf.float().contiguous().view(torch.int32), best_idx.to(torch.int32)], dim=1)
-    return torch.cat([head.contiguous().view(torch.uint8).reshape(n, 8), answers.to(torch.uint8).reshape(n, -1)], 1)
+    return torch.cat([head.contiguous().view(torch.uint8).reshape(n, 8),
+                      answers.to(torch.uint8).reshape(n, answers.shape[-1])], 1)
 
 
 def unpack_results(rows: torch.Tensor, hw: int):
@@ -51,16 +52,12 @@ def gather_results(best_conf, best_idx, answers, n_boards: int, group=None):
     return unpack_results(torch.cat(parts, 0), hw)
 
 
-def sharded_rollout(model, task, boards, rc, seed: int = 0, group=None):
-    """Every rank rolls out its shard of `boards` on its current CUDA device, selects the
-    conf@K trial per board with the library's selection kernel, and all ranks receive the
-    results of every board: dict(best_conf, best_idx, answers) as numpy arrays."""
+def _shard_results(model, task, shard, rc, seed: int, board_offset: int):
+    """Rollout of one rank's (non-empty) shard and its conf@K selection on the rank's GPU:
+    (best_conf (n,), best_idx (n,), answers (n, hw)) device tensors."""
     from .rollout import rollout
 
-    world = dist.get_world_size(group) if dist.is_initialized() else 1
-    rank = dist.get_rank(group) if dist.is_initialized() else 0
-    s, e = shard_range(len(boards), world, rank)
-    res = rollout(model, task, boards.subset(np.arange(s, e)), rc, seed=seed, board_offset=s)
+    res = rollout(model, task, shard, rc, seed=seed, board_offset=board_offset)
     eng = model._engine
     n, K, H, W = res.pred.shape
     dev = eng.device
@@ -68,6 +65,33 @@ def sharded_rollout(model, task, boards, rc, seed: int = 0, group=None):
     alive = torch.from_numpy(res.alive.astype(np.uint8)).to(dev)
     pred = torch.from_numpy(res.pred.reshape(n * K, H * W).astype(np.uint8)).to(dev)
     idx, best, ans = eng.select(conf.reshape(-1), n, K, alive=alive.reshape(-1), pred=pred, hw=H * W)
+    return best, idx, ans
+
+
+def _result_device(group) -> torch.device:
+    """Where a rank keeps the tensors it all-gathers: host memory for gloo, else its GPU."""
+    if dist.is_initialized() and dist.get_backend(group) == "gloo":
+        return torch.device("cpu")
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def sharded_rollout(model, task, boards, rc, seed: int = 0, group=None):
+    """Every rank rolls out its shard of `boards` on its current CUDA device, selects the
+    conf@K trial per board with the library's selection kernel, and all ranks receive the
+    results of every board: dict(best_conf, best_idx, answers) as numpy arrays.  A rank whose
+    shard is empty (more ranks than boards) launches nothing and joins the all-gather with
+    zero rows."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    s, e = shard_range(len(boards), world, rank)
+    H, W = boards.shape
+    if e > s:
+        best, idx, ans = _shard_results(model, task, boards.subset(np.arange(s, e)), rc, seed, s)
+    else:
+        dev = _result_device(group)
+        best = torch.zeros(0, dtype=torch.float32, device=dev)
+        idx = torch.zeros(0, dtype=torch.int32, device=dev)
+        ans = torch.zeros((0, H * W), dtype=torch.uint8, device=dev)
     if world > 1:
         best, idx, ans = gather_results(best, idx, ans, len(boards), group)
     return {

@@ -12,7 +12,9 @@ Randomness (RolloutConfig.engine["fire"]):
   "torch"            -- the reference's stream: one torch.Generator(seed) on the model's device,
                         `randn` for the initial state of each pass (src/nca/model.py:404) and one
                         `rand((B,1,H,W))` per step (src/nca/model.py:586), consumed in the same
-                        order; the kernel applies the drawn masks.
+                        order; the kernel applies the drawn masks.  engine["generator"] = "cpu"
+                        makes the draws on a CPU generator instead (copied to the device), which
+                        replays exactly the stream of a reference run on the CPU.
 
 The reference's options on this path:
   threshold adaptive firing: RolloutConfig.p_low / tau / given_confident (src/nca/model.py:
@@ -52,6 +54,10 @@ from . import _lib as L
 from .engine import B200Engine
 from .perturb import circular_masks, sample_noise
 from .tasks import Boards, Task
+
+
+# With engine["fire"] == "torch", the longest launch (steps) whose draws are made at once.
+TORCH_STEP_CHUNK = 64
 
 
 @dataclass
@@ -161,9 +167,13 @@ def rollout(model, task: Task, boards: Boards, rc, seed: int = 0, task_ids=None,
     HW = H * W
     K = rc.k
     per_pass = max(1, rc.max_cells // (K * HW))
+    gen_where = opts.get("generator", "device")
+    if gen_where not in ("device", "cpu"):
+        raise ValueError("engine['generator'] must be 'device' or 'cpu'")
+    gdev = dev if gen_where == "device" else torch.device("cpu")
     gen = None
     if fire == "torch":
-        gen = torch.Generator(device=dev)
+        gen = torch.Generator(device=gdev)
         gen.manual_seed(seed)
     rng = np.random.default_rng(seed)  # host draws: pruning orders (src/nca/rollout.py:103)
 
@@ -196,9 +206,9 @@ def rollout(model, task: Task, boards: Boards, rc, seed: int = 0, task_ids=None,
         if fire == "torch" or cfg.sigma_init != 0:
             g0 = gen
             if g0 is None:
-                g0 = torch.Generator(device=dev)
+                g0 = torch.Generator(device=gdev)
                 g0.manual_seed(seed + start)
-            x0 = torch.randn((B, cfg.channels, H, W), generator=g0, device=dev) * cfg.sigma_init
+            x0 = (torch.randn((B, cfg.channels, H, W), generator=g0, device=gdev) * cfg.sigma_init).to(dev)
             eng.load_nchw(st, x0)
             # clamp the given cells: a step where no cell fires
             zero = torch.zeros((1, B, HW), dtype=torch.uint8, device=dev)
@@ -243,15 +253,18 @@ def rollout(model, task: Task, boards: Boards, rc, seed: int = 0, task_ids=None,
                 # the reference's stream: per step a fire draw, then (inside the noise window)
                 # the noise draws; the kernel applies them
                 per_step = noise is not None and t < noise_until
-                chunks = [(t + i, 1) for i in range(n_steps)] if per_step else [(t, n_steps)]
+                # launches of at most TORCH_STEP_CHUNK steps, so that a long segment does not hold
+                # all of its draws at once; the draws stay in the reference's order
+                chunks = ([(t + i, 1) for i in range(n_steps)] if per_step else
+                          [(t0, min(TORCH_STEP_CHUNK, bnd - t0)) for t0 in range(t, bnd, TORCH_STEP_CHUNK)])
                 for t0, ns in chunks:
-                    u = torch.stack([torch.rand((Bc, 1, H, W), generator=gen, device=dev).reshape(Bc, HW)
-                                     for _ in range(ns)])
+                    u = torch.stack([torch.rand((Bc, 1, H, W), generator=gen, device=gdev).reshape(Bc, HW)
+                                     for _ in range(ns)]).to(dev)
                     nz = None
                     if per_step and t0 < noise_until:
                         tn = sample_noise(Bc, cfg.channels, H, W, noise["p_t"], noise["p_s"],
-                                          noise["sigma"], gen, dev)
-                        nz = None if tn is None else {"tensor": tn.reshape(Bc, cfg.channels, HW)}
+                                          noise["sigma"], gen, gdev)
+                        nz = None if tn is None else {"tensor": tn.reshape(Bc, cfg.channels, HW).to(dev)}
                     if rule is None:
                         eng.run(st, batch, ns, mode="mask", masks=(u < p_fire).to(torch.uint8),
                                 step0=t0, noise=nz, **kw)

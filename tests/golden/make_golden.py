@@ -3,6 +3,7 @@
 Run in a container where the reference is importable (it is not on the GPU box):
 
     PYTHONPATH=/path/to/reference/src python tests/golden/make_golden.py /path/to/reference
+    PYTHONPATH=/path/to/reference/src python tests/golden/make_golden.py /path/to/reference long
 
 Every array in the file is produced by the reference's own code: nca.model.NCA (built through
 nca.model.build_model with the benchmark overrides and the benchmark's synthetic weights loaded
@@ -224,5 +225,47 @@ def presets() -> None:
     print(f"wrote {out} ({out.stat().st_size / 1e3:.0f} kB, {len(P)} arrays)")
 
 
+def long_rollout() -> None:
+    """A long rollout for the task-level agreement check: the reference's trained maze_ood preset
+    run by the reference's own rollout() on 100 seeded 59x59 perfect mazes (a 29x29-cell maze)
+    for D = 2000 steps, the depth the reference's Table 1 uses at that size
+    (scripts/eval_maze_scaling.py:26, TABLE1 = {13: 300, 59: 2000, 201: 13000}).  K = 1, the
+    rollout's own torch.Generator(seed) on the CPU (randn initial state, one rand mask per step),
+    so a GPU run that replays the same draws sees the same fire masks.  Stored: the boards, the
+    per-board exact flags, the decoded final boards, the board confidences and update counts."""
+    from nca.rollout import RolloutConfig, rollout, score_candidates  # noqa: E402
+    from nca.tasks.base import Boards as RefBoards  # noqa: E402
+    from nca.tasks.maze import MazeOOD  # noqa: E402
+    from nca.train import load_model  # noqa: E402
+
+    torch.set_num_threads(8)
+    m, _ = load_model(REF / "runs" / "engine" / "maze_ood_opt" / "seed0" / "final.pt", device="cpu")
+    rng = np.random.default_rng(LONG_BOARD_SEED)
+    pairs = [generate_perfect_maze(LONG_SIZE, rng) for _ in range(LONG_N)]
+    inputs = np.stack([a for a, _ in pairs]).astype(np.int64)
+    targets = np.stack([b for _, b in pairs]).astype(np.int64)
+    boards = RefBoards(inputs, targets, inputs != 0)
+    task = MazeOOD()
+    rc = RolloutConfig(depth=LONG_DEPTH, k=1, record_every=LONG_DEPTH // 4)
+    res = rollout(m, task, boards, rc, seed=LONG_ROLLOUT_SEED)
+    met = score_candidates(task, res, boards)
+    P = dict(inputs=inputs.astype(np.uint8), targets=targets.astype(np.uint8),
+             exact=np.asarray(met["exact"]).reshape(LONG_N).astype(bool),
+             pred=res.pred[:, 0].astype(np.uint8), conf=res.conf[:, 0],
+             updates=res.cell_updates[:, 0], trace_exact=res.trace_exact[:, 0],
+             steps=res.steps, depth=np.array(LONG_DEPTH), rollout_seed=np.array(LONG_ROLLOUT_SEED),
+             board_seed=np.array(LONG_BOARD_SEED))
+    out = OUT.parent / "long_rollout.npz"
+    np.savez_compressed(out, **P)
+    print(f"wrote {out} ({out.stat().st_size / 1e3:.0f} kB); reference exact rate "
+          f"{P['exact'].mean():.3f}, trace {res.trace_exact[:, 0].mean(0)}")
+
+
+LONG_N, LONG_SIZE, LONG_DEPTH = 100, 59, 2000
+LONG_BOARD_SEED, LONG_ROLLOUT_SEED = 71, 5
+
 if __name__ == "__main__":
-    main()
+    if len(sys.argv) > 2 and sys.argv[2] == "long":
+        long_rollout()
+    else:
+        main()

@@ -92,3 +92,58 @@ def test_failed_rank_is_reported_by_the_others():
     assert out[1][1] == "error"
     # rank 0's collective ends with an error (peer gone / timeout) instead of hanging
     assert out[0][1] == "error"
+
+
+def _sharded_worker(rank, world, port, n_boards, q):
+    """sharded_rollout with the per-shard GPU work replaced by a host fake: checks the host
+    logic around it (shard ranges, empty shards, the all-gather) on gloo ranks."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+
+    import ncas_b200.distributed as D
+    from ncas_b200.tasks import sudoku_boards
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    calls = []
+
+    def fake(model, task, shard, rc, seed, board_offset):
+        calls.append(len(shard))
+        ids = torch.arange(board_offset, board_offset + len(shard))
+        ans = torch.from_numpy(shard.inputs.reshape(len(shard), -1).astype(np.uint8))
+        return ids.float() / 4, (ids % 3).to(torch.int32), ans
+
+    D._shard_results = fake
+    try:
+        boards = sudoku_boards(n_boards, seed=1)
+        out = D.sharded_rollout(None, None, boards, None, seed=0)
+        q.put((rank, calls, out["best_conf"], out["best_idx"], out["answers"]))
+    except Exception as ex:  # noqa: BLE001
+        q.put((rank, "error", type(ex).__name__, str(ex)[:200], None))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_more_ranks_than_boards_gives_empty_shards_that_still_gather():
+    world, n_boards = 3, 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_sharded_worker, args=(r, world, port, n_boards, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    out = sorted([q.get(timeout=120) for _ in range(world)], key=lambda t: t[0])
+    for p in ps:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    from ncas_b200.tasks import sudoku_boards
+
+    boards = sudoku_boards(n_boards, seed=1)
+    ids = np.arange(n_boards)
+    for rank, calls, conf, idx, ans in out:
+        assert calls != "error", (calls, conf, idx)
+        # ranks 0 and 1 hold one board each; rank 2's shard is empty and does no shard work
+        assert calls == ([] if rank == 2 else [1])
+        np.testing.assert_allclose(conf, ids / 4)
+        assert np.array_equal(idx, ids % 3)
+        assert np.array_equal(ans, boards.inputs.astype(np.uint8))

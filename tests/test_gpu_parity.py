@@ -178,6 +178,11 @@ def test_select_matches_oracle():
     conf[:, 5] = conf[:, 9]  # ties: first index wins
     alive = rng.random((N, K)) < 0.7
     alive[7] = False  # no alive trial: index 0, like np.argmax over -inf
+    # diverged trials: np.argmax returns the first alive NaN; a dead NaN is ignored
+    conf[11, [3, 40]] = np.nan
+    alive[11, [3, 40]] = True
+    conf[12, 2] = np.nan
+    alive[12, 2] = False
     pred = rng.integers(0, 10, (N * K, 81), dtype=np.uint8)
     m = build("sudoku", seed=0, device=DEV)
     eng = m.engine()
@@ -188,8 +193,8 @@ def test_select_matches_oracle():
         assert np.array_equal(idx.cpu().numpy(), want)
         assert np.array_equal(bp.cpu().numpy(), pred.reshape(N, K, 81)[np.arange(N), want])
         got = best.cpu().numpy()
-        ref = np.where(alive[:, :k], conf[:, :k], -np.inf).max(1)
-        assert np.array_equal(got, ref.astype(np.float32))
+        ref = np.where(alive[:, :k], conf[:, :k], -np.inf)[np.arange(N), want]
+        assert np.array_equal(got, ref.astype(np.float32), equal_nan=True)
 
 
 def test_prune_refill_matches_oracle():

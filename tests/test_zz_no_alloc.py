@@ -1,6 +1,6 @@
-"""nca_b200_run_steps_static: NCA steps for callers that cannot allocate device memory (code
-inside a CUDA graph being built, a framework whose allocator owns all device memory, a runtime
-with a fixed memory budget).  Its scratch is a static device array in the library; these checks
+"""nca_b200_run_steps_static: NCA steps for callers that cannot allocate device memory (a
+framework whose allocator owns all device memory, a runtime with a device-memory budget fixed at
+start-up).  Its scratch is a static device array in the library; these checks
 call it through the C ABI and compare it with the allocating path (nca_b200_run_steps on a
 caller-allocated state workspace), on two calls in a row with different inputs, so that a call
 cannot pass by reusing what the previous call left in the shared array."""

@@ -52,3 +52,13 @@ def test_metrics_exact_and_cell_acc():
     m = task.metrics(pred, b)
     assert m["exact"].tolist() == [True, False, True]
     assert m["cell_acc"][1] == 0 and m["valid"][0]
+
+
+def test_long_rollout_boards_match_reference_generator():
+    """The 59x59 boards of the long-rollout fixture (drawn by the reference's
+    generate_perfect_maze) come out of our generator for the same seed."""
+    from pathlib import Path
+
+    L = np.load(Path(__file__).resolve().parent / "golden" / "long_rollout.npz")
+    b = T.maze_boards(len(L["inputs"]), L["inputs"].shape[1], seed=int(L["board_seed"]), goal=False)
+    assert np.array_equal(b.inputs, L["inputs"]) and np.array_equal(b.targets, L["targets"])

@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define NCA_B200_ABI_VERSION 2
+#define NCA_B200_ABI_VERSION 3
 #define NCA_B200_MAX_OUT 16   /* maximum number of readout tokens (n_out) and readout channels */
 
 typedef enum NcaStatus {
@@ -120,6 +120,9 @@ typedef struct NcaState {
                                nca_b200_state_bind and nca_b200_state_load_nchw) */
   uint32_t* tile_steps;     /* device [n_tiles]: per-tile step counters of a launch (the step
                                kernel's dependencies between neighbouring tiles) */
+  float* fire_p;            /* device [n_tiles * 128]: per cell, the fire probability of the next
+                               step under the confidence rules (fire modes 2..5), written before
+                               and during a launch */
 } NcaState;
 
 typedef enum NcaNoiseMode {

@@ -15,7 +15,7 @@ LIB_DIR = Path(__file__).resolve().parent / "_lib"
 LIB_PATH = LIB_DIR / "libnca_b200.so"
 
 MAX_OUT = 16
-ABI_VERSION = 2  # NCA_B200_ABI_VERSION of include/nca_b200.h
+ABI_VERSION = 3  # NCA_B200_ABI_VERSION of include/nca_b200.h
 
 NCA_OK = 0
 STATUS_NAMES = {
@@ -86,6 +86,7 @@ class NcaState(C.Structure):
         ("cur", C.c_int32),
         ("clamped", C.c_int32),
         ("tile_steps", C.c_void_p),
+        ("fire_p", C.c_void_p),
     ]
 
 

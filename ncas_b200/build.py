@@ -21,6 +21,9 @@ SOURCES = [CSRC / "api.cu", CSRC / "steps_64_256.cu", CSRC / "steps_32_128.cu",
 HEADERS = [CSRC / "ptx.cuh", CSRC / "step_kernel.cuh", CSRC / "launch.cuh",
            ROOT.parent / "include" / "nca_b200.h"]
 DEPS = SOURCES + HEADERS
+# the torch operators over the C ABI (ncas_b200._ops), linked against libnca_b200.so
+OPS_SOURCE = CSRC / "torch_ops.cpp"
+OPS_OUT = ROOT / "_lib" / "libnca_b200_ops.so"
 
 ARCH_FLAGS = [
     "-gencode",
@@ -42,10 +45,23 @@ def nvcc() -> str:
 
 
 def up_to_date() -> bool:
-    if not OUT.exists():
+    if not OUT.exists() or not OPS_OUT.exists():
         return False
-    t = OUT.stat().st_mtime
-    return all(p.stat().st_mtime <= t for p in DEPS if p.exists())
+    t = min(OUT.stat().st_mtime, OPS_OUT.stat().st_mtime)
+    return all(p.stat().st_mtime <= t for p in DEPS + [OPS_SOURCE] if p.exists())
+
+
+def _torch_flags() -> tuple[list[str], list[str]]:
+    """Compile and link flags of a C++ file against this interpreter's torch."""
+    import torch
+    from torch.utils import cpp_extension
+
+    inc = [f"-I{p}" for p in cpp_extension.include_paths()] + ["-I/usr/local/cuda/include"]
+    abi = f"-D_GLIBCXX_USE_CXX11_ABI={int(torch.compiled_with_cxx11_abi())}"
+    tlib = str(Path(torch.__file__).resolve().parent / "lib")
+    libs = [f"-L{tlib}", "-ltorch", "-ltorch_cpu", "-lc10", "-lc10_cuda", "-ltorch_cuda",
+            f"-Wl,-rpath,{tlib}"]
+    return [abi, *inc], libs
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
@@ -63,6 +79,10 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         cmd = [nvcc(), *ARCH_FLAGS, *extra, "-c", "-o", str(obj), str(src)]
         procs.append((cmd, obj, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE,
                                                  text=True)))
+    cflags, libs = _torch_flags()
+    ops_obj = objdir / "torch_ops.o"
+    ops_cmd = ["g++", "-O2", "-std=c++17", "-fPIC", *cflags, "-c", "-o", str(ops_obj), str(OPS_SOURCE)]
+    ops_proc = subprocess.Popen(ops_cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
     objs = []
     for cmd, obj, p in procs:
         out, err = p.communicate()
@@ -77,6 +97,16 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if res.returncode != 0:
         raise RuntimeError(f"nvcc link failed ({' '.join(cmd)}):\n{res.stdout}\n{res.stderr}")
     tmp.replace(OUT)
+    out, err = ops_proc.communicate()
+    if ops_proc.returncode != 0:
+        raise RuntimeError(f"g++ failed ({' '.join(ops_cmd)}):\n{out}\n{err}")
+    tmp = OPS_OUT.with_suffix(".so.tmp")
+    cmd = ["g++", "-shared", "-o", str(tmp), str(ops_obj), f"-L{OUT.parent}", "-lnca_b200",
+           "-Wl,-rpath,$ORIGIN", *libs]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"link of the torch operators failed ({' '.join(cmd)}):\n{res.stdout}\n{res.stderr}")
+    tmp.replace(OPS_OUT)
     return OUT
 
 

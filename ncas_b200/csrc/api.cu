@@ -238,6 +238,36 @@ __global__ void readout_kernel(const float* master, const uint16_t* mirror, NcaB
   }
 }
 
+// Fire probability of every cell of the current state under the confidence rules (the values
+// the step kernel's epilogue then keeps up to date): head_readout of the cell's readout slice,
+// then the continuous or the threshold rule (src/nca/model.py:566-593).  One thread per cell of
+// the tiled layout; rows past the last cell get 0.
+__global__ void fire_p_kernel(const float* master, const uint16_t* mirror, int C, long long n_cells,
+                              long long total, int hw, NcaBatchDesc b, ReadoutArgs R, int mode,
+                              float scale, float bias, float p_low, float tau, float p_fire,
+                              int given_confident, float* fire_p) {
+  const long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= n_cells) return;
+  if (g >= total) {
+    fire_p[g] = 0.f;
+    return;
+  }
+  const int inst = (int)(g / hw);
+  const int p = (int)(g - (long long)inst * hw);
+  const int row = b.inst_row ? b.inst_row[inst] : inst / b.trials;
+  float xo[16];
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    xo[c] = 0.f;
+    if (c < R.c_out) xo[c] = state_get(master, mirror, C, g, R.out_off + c);
+  }
+  float conf;
+  int arg;
+  head_readout(R.head_kind, R.n_out, R.c_out, R.head_w, R.head_b, xo, conf, arg);
+  fire_p[g] = adaptive_prob(mode, conf, b.given[(long long)row * hw + p] != 0, scale, bias, p_low, tau,
+                            p_fire, given_confident);
+}
+
 // Order of np.argmax over (alive ? conf : -inf): a NaN is larger than every number (argmax
 // returns the first NaN), ties go to the smaller index.
 __device__ __forceinline__ bool select_better(float v, int k, float bv, int bi) {
@@ -571,7 +601,8 @@ int32_t nca_b200_state_bytes(int32_t n_inst, int32_t hw, int32_t channels, int32
   const bool hl = hilo_layout(channels, precision == NCA_PREC_BF16);
   const size_t master = align256((size_t)tiles * kTileM * channels * (hl ? 2 : 4));
   const size_t mirror = precision == NCA_PREC_BF16 ? align256((size_t)tiles * kTileM * channels * 2) : 0;
-  *bytes = 2 * master + 2 * mirror + align256((size_t)tiles * 4);  // + per-tile step counters
+  // + per-tile step counters + per-cell fire probabilities (confidence rules)
+  *bytes = 2 * master + 2 * mirror + align256((size_t)tiles * 4) + align256((size_t)tiles * kTileM * 4);
   return NCA_OK;
 }
 
@@ -598,6 +629,7 @@ int32_t nca_b200_state_bind(NcaState* st, void* buffer, size_t bytes, int32_t n_
   st->mirror[0] = mirror ? reinterpret_cast<uint16_t*>(p + 2 * master) : nullptr;
   st->mirror[1] = mirror ? reinterpret_cast<uint16_t*>(p + 2 * master + mirror) : nullptr;
   st->tile_steps = reinterpret_cast<uint32_t*>(p + 2 * master + 2 * mirror);
+  st->fire_p = reinterpret_cast<float*>(p + 2 * master + 2 * mirror + align256((size_t)tiles * 4));
   st->cur = 0;
   st->clamped = 0;
   return NCA_OK;
@@ -659,7 +691,37 @@ int32_t nca_b200_run_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaStat
   if (fire->noise_mode == NCA_NOISE_EXTERNAL && (!fire->noise || n_steps != 1)) return NCA_ERR_INVALID;
   const bool noise = fire->noise_mode != NCA_NOISE_NONE;
   const bool adaptive = fire->mode >= NCA_FIRE_ADAPTIVE_PHILOX;  // fire decisions on the confidence
+  if (adaptive) {
+    // The epilogue part that computes the next step's fire probability must hold the whole
+    // readout slice.
+    const int ch = epi_part_channels(C);
+    if (m->out_offset / ch != (m->out_offset + m->c_out - 1) / ch) return NCA_ERR_UNSUPPORTED;
+  }
+  // Fire probabilities of the current state for the first step of each launch (the step kernel
+  // keeps them up to date for the following steps).
+  auto init_fire_p = [&]() -> int32_t {
+    ReadoutArgs R;
+    memset(&R, 0, sizeof(R));
+    R.C = st->channels;
+    R.hw = st->hw;
+    R.n_inst = st->n_inst;
+    R.c_out = m->c_out;
+    R.out_off = m->out_offset;
+    R.n_out = m->n_out;
+    R.head_kind = m->head_kind;
+    copy_head(R.head_w, R.head_b, m->head_w, m->head_b, m->n_out, m->c_out);
+    const long long cells = st->n_tiles * kTileM;
+    fire_p_kernel<<<(unsigned)((cells + 255) / 256), 256, 0, s>>>(
+        st->master[st->cur], st->mirror[st->cur], st->channels, cells, (long long)st->n_inst * st->hw,
+        st->hw, *b, R, fire->mode, fire->adapt_scale, fire->adapt_bias, fire->p_low, fire->tau,
+        fire->p_fire, fire->given_confident, st->fire_p);
+    return cuda_status(cudaGetLastError());
+  };
   auto launch = [&](int32_t n, const NcaFireDesc* f) -> int32_t {
+    if (adaptive) {
+      const int32_t r = init_fire_p();
+      if (r != NCA_OK) return r;
+    }
     // the benchmark models (32, 128), (64, 256) and the reference's maze presets (16, 128),
     // (32, 256) (maze_ood, maze_hard: src/nca/model.py:656-700)
     if (C == 32 && HD == 128) return launch_shape_32_128(split, noise, adaptive, m, b, st, n, f, ctrl, timeout_ms, s);
@@ -702,8 +764,7 @@ int32_t nca_b200_readout(const NcaModelDesc* m, const NcaBatchDesc* b, const Nca
   R.out_off = m->out_offset;
   R.n_out = m->n_out;
   R.head_kind = m->head_kind;
-  memcpy(R.head_w, m->head_w, sizeof(R.head_w));
-  memcpy(R.head_b, m->head_b, sizeof(R.head_b));
+  copy_head(R.head_w, R.head_b, m->head_w, m->head_b, m->n_out, m->c_out);
   memcpy(R.out_tokens, m->out_tokens, sizeof(R.out_tokens));
   readout_kernel<<<st->n_inst, 128, 0, as_stream(stream)>>>(st->master[st->cur], st->mirror[st->cur], *b, R, pred,
                                                            cell_conf, board_conf, targets,

@@ -43,8 +43,7 @@ inline int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaSta
   A.n_out = m->n_out;
   A.fixed_taps = m->fixed_taps;
   memcpy(A.taps, m->taps, sizeof(A.taps));
-  memcpy(A.head_w, m->head_w, sizeof(A.head_w));
-  memcpy(A.head_b, m->head_b, sizeof(A.head_b));
+  copy_head(A.head_w, A.head_b, m->head_w, m->head_b, m->n_out, m->c_out);
   A.wimg = reinterpret_cast<const uint8_t*>(m->weights);
   A.wimg_lo = (st->precision == NCA_PREC_SPLIT) ? reinterpret_cast<const uint8_t*>(m->weights_lo) : nullptr;
   A.head_kind = m->head_kind;
@@ -83,10 +82,10 @@ inline int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaSta
   // Window stages: in the hi/lo layout a window lives from the stencil to the epilogue (which
   // reads the hi part of the old state from it), so more stages keep the stencil ahead.
   int stages = Cfg::HILO ? kMaxStages : 2;
-  int smem = SmemLayout<Cfg>(stages, A.win_cells, A.wimg_lo != nullptr).total + 1024;
+  int smem = SmemLayout<Cfg>(stages, A.win_cells, A.wimg_lo != nullptr, A.c_out).total + 1024;
   while (smem > kMaxSmem && stages > 1) {
     --stages;
-    smem = SmemLayout<Cfg>(stages, A.win_cells, A.wimg_lo != nullptr).total + 1024;
+    smem = SmemLayout<Cfg>(stages, A.win_cells, A.wimg_lo != nullptr, A.c_out).total + 1024;
   }
   if (smem > kMaxSmem) return NCA_ERR_UNSUPPORTED;
   A.stages = stages;
@@ -107,7 +106,9 @@ inline int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaSta
   auto kern = tiledep ? nca_step_kernel<CfgTD> : nca_step_kernel<Cfg>;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return NCA_ERR_CUDA;
+
   A.tile_steps = tiledep ? st->tile_steps : nullptr;
+  A.fire_p = st->fire_p;
   if (tiledep) {
     e = cudaMemsetAsync(st->tile_steps, 0, (size_t)st->n_tiles * sizeof(uint32_t), stream);
     if (e != cudaSuccess) return NCA_ERR_CUDA;
@@ -116,10 +117,10 @@ inline int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaSta
   if (e != cudaSuccess) return NCA_ERR_CUDA;
   if (n_steps > 1) {
     void* args[] = {&A};
-    e = cudaLaunchCooperativeKernel((const void*)kern, dim3(grid), dim3(kThreads), args,
+    e = cudaLaunchCooperativeKernel((const void*)kern, dim3(grid), dim3(Cfg::THREADS), args,
                                     (size_t)smem, stream);
   } else {
-    kern<<<grid, kThreads, smem, stream>>>(A);
+    kern<<<grid, Cfg::THREADS, smem, stream>>>(A);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) return NCA_ERR_CUDA;

@@ -28,16 +28,20 @@
 namespace nca {
 
 constexpr int kTileM = 128;
-constexpr int kNumWarps = 18;       // 0 MMA, 1 loader, 2..9 stencil, 10..17 epilogue
-constexpr int kThreads = kNumWarps * 32;
-constexpr int kStencilWarp0 = 2;
-constexpr int kEpiWarp0 = 10;
+// Warp roles: warp group 0 holds the MMA warp (0), the loader warp (1) and two idle warps; warp
+// groups 1-2 the 8 stencil warps (4..11); warp groups 3.. the epilogue warps (12..).  With 28
+// warps a sub-partition hosts 7 of them, so every thread has 72 registers.
+constexpr int kStencilWarp0 = 4;
+constexpr int kEpiWarp0 = 12;
 
 constexpr int pow2ceil(int v) {
   int p = 32;
   while (p < v) p <<= 1;
   return p;
 }
+
+// Channels of one epilogue thread in E2 (two epilogue parts split the channels).
+__host__ __device__ constexpr int epi_part_channels(int C) { return C / 2; }
 
 // State layout of a model (see state_get): bf16 mode keeps hi + lo bf16 parts when C >= 64 (the
 // MMA work per cell hides the extra packing, and a step moves 512 instead of 768 bytes per
@@ -49,8 +53,8 @@ template <int C_, int HD_, bool SPLIT_, bool NOISE_ = false, bool TILEDEP_ = fal
 struct StepCfg {
   static constexpr int C = C_;
   static constexpr bool NOISE = NOISE_;  // test-time state noise (a separate instantiation)
-  // fire decisions on the cell's confidence (fire modes 2..5), evaluated by all 8 stencil warps
-  // after z; the other modes draw them in the half-0 stencil warps before z
+  // fire decisions on the cell's confidence (fire modes 2..5): the epilogue computes each cell's
+  // fire probability for the next step from the values it stores, the stencil draws against it
   static constexpr bool ADAPTIVE = ADAPTIVE_;
   // steps ordered by per-tile step counters (StepArgs::tile_steps) instead of a grid barrier
   static constexpr bool TILEDEP = TILEDEP_;
@@ -79,11 +83,23 @@ struct StepCfg {
   static constexpr int ACC2_COL = ACC_COL + (H_IN_ACC ? HD / 4 : 0);
   static constexpr int W1_BYTES = HD * P * 2;
   static constexpr int W2_BYTES = C * HD * 2;
+  // Epilogue warps per tensor-memory lane quarter ("parts"): 2, each with E1 of one GEMM1
+  // N-half and E2 of half of the channels.  The code also runs with 4 parts (two per N-half,
+  // the second writing h after the first has read its accumulator columns): measured slower at
+  // 72 registers per thread, the limit of 28 warps.
+  static constexpr int EPI_PARTS = 2;
+  static_assert(C_ / EPI_PARTS == epi_part_channels(C_), "epilogue channel shares");
+  static constexpr int PARTS_PER_HALF = EPI_PARTS / 2;
+  static constexpr int EPI_WARPS = 4 * EPI_PARTS;
+  static constexpr int CH = C_ / EPI_PARTS;             // channels of one epilogue thread in E2
+  static constexpr int NUM_WARPS = kEpiWarp0 + EPI_WARPS;
+  static constexpr int THREADS = NUM_WARPS * 32;
   static_assert(ACC_COL + NACC * HD <= 512, "tensor memory budget");
   static_assert(C % 16 == 0 && HD % 32 == 0 && HD <= 256 && P % 64 == 0 && HD % 64 == 0,
                 "shape constraints of the UMMA tiles");
   static_assert(NCH % 2 == 0, "stencil channel halves");
   static_assert(!H_IN_ACC || C <= HD / 4, "acc2 must fit next to h in the accumulator region");
+  static_assert(NUM_WARPS % 4 == 0 && CH % 8 == 0, "warp groups and E2 channel shares");
 };
 
 // n / d for 0 <= n < 2^31 with a multiply-high and a shift (Granlund & Montgomery, "Division by
@@ -139,25 +155,34 @@ struct StepArgs {
   long long noise_until;
   const float* noise;
   unsigned* tile_steps;  // per tile: steps of this launch whose stores are complete (TILEDEP)
+  float* fire_p;         // per cell: fire probability of the next step (adaptive rules)
   int* ctrl;
   unsigned long long timeout_ns;
 };
 
+constexpr int kBarSlots = 48;  // mbarriers in the shared-memory layout
+constexpr int kSliceSlots = 1;  // adaptive rules: readout-slice buffers between epilogue and confidence warps
+
 // Shared-memory layout (offsets from a 1024-byte aligned base).
 template <class Cfg>
 struct SmemLayout {
-  int w1, w2, w1lo, w2lo, win, b1, b2, flags, bars, misc, total;
-  __host__ __device__ SmemLayout(int stages, int win_cells, bool lo) {
+  int w1, w2, w1lo, w2lo, win, pwin, slice, b1, b2, flags, bars, misc, total;
+  // c_out: readout channels (the adaptive rules keep each row's readout slice here)
+  __host__ __device__ SmemLayout(int stages, int win_cells, bool lo, int c_out) {
     w1 = 0;
     w2 = w1 + Cfg::W1_BYTES;
     w1lo = w2 + Cfg::W2_BYTES;  // the residual image, when present, follows (same layout)
     w2lo = w1lo + Cfg::W1_BYTES;
     win = ((lo ? w2lo + Cfg::W2_BYTES : w1lo) + 1023) & ~1023;
-    b1 = (win + stages * (win_cells + 1) * Cfg::ROWB + 15) & ~15;  // + the padding cell
+    pwin = (win + stages * (win_cells + 1) * Cfg::ROWB + 15) & ~15;  // + the padding cell
+    // adaptive rules: the tile's fire probabilities, one fp32 per row, with each window stage,
+    // and the epilogue's copy of each row's new readout slice (c_out fp32 per row)
+    slice = pwin + (Cfg::ADAPTIVE ? stages * kTileM * 4 : 0);
+    b1 = slice + (Cfg::ADAPTIVE ? kSliceSlots * kTileM * (c_out + 1) * 4 : 0);  // + the row's given flag
     b2 = b1 + Cfg::HD * 4;
     flags = b2 + Cfg::C * 4;
     bars = (flags + 4 * kTileM + 7) & ~7;
-    misc = bars + 32 * 8;  // BAR_COUNT <= 32 barriers
+    misc = bars + kBarSlots * 8;
     total = misc + 64;
   }
 };
@@ -183,14 +208,19 @@ enum BarId {
   BAR_WEIGHTS = 24,
   BAR_DRAIN = 25,
   BAR_FLAGS = 26,       // +ring index (4): per-row fire/given flags of a tile are written
-  BAR_COUNT = 30
+  // +lane quarter + 4 * GEMM1 half (8): the first epilogue part of a half has read its
+  // accumulator columns (bf16 mode, two parts per half: the second part writes h over them)
+  BAR_PAIR = 30,
+  BAR_SLICE_FULL = 38,   // +slot (2): adaptive rules, the epilogue has written a tile's readout slices
+  BAR_SLICE_EMPTY = 40,  // +slot (2): the confidence warps have read them
+  BAR_COUNT = 42
 };
-static_assert(BAR_COUNT <= 32, "barrier area of the shared-memory layout");
+static_assert(BAR_COUNT <= kBarSlots, "barrier area of the shared-memory layout");
 
 // Failure sites reported in ctrl[1].
 enum Where {
   W_MMA_ZFULL = 1, W_MMA_ACCEMPTY, W_MMA_HFULL, W_MMA_WEIGHTS, W_LOAD_EMPTY, W_LOAD_GRID,
-  W_ST_WINFULL, W_ST_ZEMPTY, W_E1_ACC, W_E2_ACC2, W_DRAIN, W_E2_FLAGS, W_PUBLISH
+  W_ST_WINFULL, W_ST_ZEMPTY, W_E1_ACC, W_E2_ACC2, W_DRAIN, W_E2_FLAGS, W_PUBLISH, W_E1_PAIR, W_CONF
 };
 
 // A window stage is laid out [chunk][window cell][16 B]: lanes that read the same chunk of
@@ -295,36 +325,38 @@ __device__ __forceinline__ void state_put(float* master, uint16_t* mirror, int C
 // kind 0 (head "mlp"): scores head_w x + head_b, confidence the max softmax;
 // kind 1 (head "l2"): rows of head_w are the output-token embeddings e_o, score
 // 1 / (1 + sqrt(|x - e_o|^2 + 1e-8)), confidence the best score.  arg is the first best token
-// (torch.argmax).  The loops run to the compile-time maximum with uniform exits, so the slice
-// stays in registers.
+// (torch.argmax).  head_w and head_b are zero outside n_out x c_out and xs is zero from c_out on
+// (copy_head on the host, the callers' slices), so every row sums all 16 channels without a check
+// per channel: the extra terms are exact zeros and leave each score as the sum over c < c_out in
+// increasing order.  Only the rows o < n_out are evaluated.
 __device__ __forceinline__ void head_readout(int kind, int n_out, int c_out, const float (&hw)[16][16],
                                              const float (&hb)[16], const float (&xs)[16],
                                              float& conf, int& arg) {
-  auto score = [&](int o) {
-    if (kind == 1) {
-      float d2 = 0.f;
+  (void)c_out;
+  float sc[16];
+  float best = -3.402823466e38f;
+  int a = 0;
 #pragma unroll
-      for (int c = 0; c < 16; ++c)
-        if (c < c_out) {
+  for (int o = 0; o < 16; ++o) {
+    sc[o] = 0.f;
+    if (o < n_out) {
+      float v;
+      if (kind == 1) {
+        float d2 = 0.f;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
           const float d = xs[c] - hw[o][c];
           d2 = fmaf(d, d, d2);
         }
-      return 1.f / (1.f + sqrtf(d2 + 1e-8f));
+        v = 1.f / (1.f + sqrtf(d2 + 1e-8f));
+      } else {
+        v = hb[o];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) v = fmaf(hw[o][c], xs[c], v);
+      }
+      sc[o] = v;
+      if (v > best || o == 0) { best = v; a = o; }
     }
-    float a = hb[o];
-#pragma unroll
-    for (int c = 0; c < 16; ++c)
-      if (c < c_out) a = fmaf(hw[o][c], xs[c], a);
-    return a;
-  };
-  float best = -3.402823466e38f;
-  int a = 0;
-  float sc[16];
-#pragma unroll
-  for (int o = 0; o < 16; ++o) {
-    if (o >= n_out) break;
-    sc[o] = score(o);
-    if (sc[o] > best || o == 0) { best = sc[o]; a = o; }
   }
   arg = a;
   if (kind == 1) {
@@ -333,59 +365,37 @@ __device__ __forceinline__ void head_readout(int kind, int n_out, int c_out, con
   }
   float den = 0.f;
 #pragma unroll
-  for (int o = 0; o < 16; ++o) {
-    if (o >= n_out) break;
-    den += expf(sc[o] - best);
-  }
+  for (int o = 0; o < 16; ++o)
+    if (o < n_out) den += expf(sc[o] - best);
   conf = fminf(fmaxf(1.f / den, 0.f), 1.f);
 }
 
-// Adaptive firing of one cell at step s on the reference's confidence (head_readout of the
-// cell's fp32 state): the continuous rule p = scale * (1 - conf) + bias, or the reference's
-// threshold rule (src/nca/model.py:566-593) p = p_low for confident cells (conf > tau, or given
-// cells when given_confident), else p_fire; fire when u < p with u from Philox or the caller.
-// Read from the state of the step's input buffer (the cell's own tile has stored step s-1: the
-// loader waited for it before loading the tile's window).
-// xhi: in the hi/lo layout, the hi parts of the readout slice (read from the window stage by
-// the caller while the stage is still its own); the lo parts come from global memory.
-template <class Cfg>
-__device__ __forceinline__ bool adaptive_fire(const StepArgs& A, int s, long long t, int m, int inst,
-                                              int p, bool given, const float (&xhi)[16]) {
-  const float* xin = A.master[(A.cur + s) & 1];
-  const long long g = t * kTileM + m;
-  float xs[16];
-#pragma unroll
-  for (int c = 0; c < 16; ++c) {
-    xs[c] = 0.f;
-    if (c < A.c_out) {
-      const int cc = A.out_off + c;
-      if constexpr (Cfg::HILO) {
-        xs[c] = xhi[c] + bf16_bits_to_f32(__ldg(reinterpret_cast<const unsigned short*>(xin) + sidx8(g, Cfg::C, cc)));
-      } else {
-        xs[c] = __ldg(xin + sidx4(g, Cfg::C, cc));
-      }
-    }
+// The head weights of a model as the kernels read them: head_w / head_b zero outside
+// n_out x c_out (head_readout sums over all 16 channels of every row).
+__host__ __forceinline__ void copy_head(float (&dw)[16][16], float (&db)[16], const float (&sw)[16][16],
+                                        const float (&sb)[16], int n_out, int c_out) {
+  for (int o = 0; o < 16; ++o) {
+    db[o] = o < n_out ? sb[o] : 0.f;
+    for (int c = 0; c < 16; ++c) dw[o][c] = (o < n_out && c < c_out) ? sw[o][c] : 0.f;
   }
-  float conf;
-  int arg;
-  head_readout(A.head_kind, A.n_out, A.c_out, A.head_w, A.head_b, xs, conf, arg);
-  float prob;
-  if (A.fire_mode >= 4)  // threshold rule: confident cells fire at p_low
-    prob = (conf > A.tau || (given && A.given_confident)) ? A.p_low : A.p_fire;
-  else
-    prob = A.ad_scale * (1.f - conf) + A.ad_bias;
-  const bool ext = A.fire_mode == 3 || A.fire_mode == 5;
-  const float u = ext ? A.uniforms[((long long)s * A.n_inst + inst) * A.HW + p]
-                      : philox_uniform(A.seed, A.inst_offset + (A.inst_id ? A.inst_id[inst] : inst), p, A.step0 + s);
-  return u < prob;
+}
+
+// The fire probability of a cell under the confidence rules: fire modes 2 and 3 the continuous
+// rule p = scale * (1 - conf) + bias, modes 4 and 5 the reference's threshold rule
+// (src/nca/model.py:566-593): p_low for confident cells (conf > tau, or given cells when
+// given_confident), else p_fire.
+__device__ __forceinline__ float adaptive_prob(int mode, float conf, bool given, float scale, float bias,
+                                               float p_low, float tau, float p_fire, int given_confident) {
+  if (mode >= 4) return (conf > tau || (given && given_confident)) ? p_low : p_fire;
+  return scale * (1.f - conf) + bias;
 }
 
 template <class Cfg>
-__global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_constant__ StepArgs A) {
+__global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_constant__ StepArgs A) {
   using namespace nca;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  const SmemLayout<Cfg> L(A.stages, A.win_cells, A.wimg_lo != nullptr);
+  const SmemLayout<Cfg> L(A.stages, A.win_cells, A.wimg_lo != nullptr, A.c_out);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L.misc);
   int* abort_flag = reinterpret_cast<int*>(smem + L.misc + 8);
@@ -409,9 +419,9 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
     *s_tiles_done = 0;
     for (int s = 0; s < kMaxStages; ++s) {
       mbar_init(&bars[BAR_WIN_FULL + s], 1);
-      // released by the 8 stencil warps, or in bf16 mode by the 8 epilogue warps, which read
-      // the hi part of the old state from the window
-      mbar_init(&bars[BAR_WIN_EMPTY + s], 8);
+      // released by the 8 stencil warps, or in the hi/lo layout by the epilogue warps, which
+      // read the hi part of the old state from the window
+      mbar_init(&bars[BAR_WIN_EMPTY + s], Cfg::HILO ? Cfg::EPI_WARPS : 8);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars[BAR_Z_FULL + s], 8);
@@ -420,21 +430,25 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
     for (int r = 0; r < 2; ++r) {
       mbar_init(&bars[BAR_ACC_FULL + r], 1);
       mbar_init(&bars[BAR_ACC_FULL_B + r], 1);
-      mbar_init(&bars[BAR_H_FULL + r], 4);
-      mbar_init(&bars[BAR_H_FULL_B + r], 4);
+      mbar_init(&bars[BAR_H_FULL + r], 4 * Cfg::PARTS_PER_HALF);
+      mbar_init(&bars[BAR_H_FULL_B + r], 4 * Cfg::PARTS_PER_HALF);
       mbar_init(&bars[BAR_ACC2_FULL + r], 1);
-      mbar_init(&bars[BAR_ACC_EMPTY + r], 8);
+      mbar_init(&bars[BAR_ACC_EMPTY + r], Cfg::EPI_WARPS);
     }
     mbar_init(&bars[BAR_WEIGHTS], 1);
     mbar_init(&bars[BAR_DRAIN], 1);
-    // the flags of a tile come from the 4 half-0 stencil warps, or with the adaptive rules from
-    // all 8 (16 cells each)
-    for (int r = 0; r < 4; ++r) mbar_init(&bars[BAR_FLAGS + r], Cfg::ADAPTIVE ? 8 : 4);
+    // the flags of a tile come from the 4 half-0 stencil warps
+    for (int r = 0; r < 4; ++r) mbar_init(&bars[BAR_FLAGS + r], 4);
+    for (int r = 0; r < 8; ++r) mbar_init(&bars[BAR_PAIR + r], 1);
+    for (int r = 0; r < kSliceSlots; ++r) {
+      mbar_init(&bars[BAR_SLICE_FULL + r], 4);   // the 4 epilogue warps of the part holding the slice
+      mbar_init(&bars[BAR_SLICE_EMPTY + r], 2);  // the 2 confidence warps
+    }
     fence_mbar_init();
   }
   // Every chunk row of a window stage ends with a padding cell (index win_cells): the stencil
   // reads it for neighbours outside the board, so no load is predicated.
-  for (int i = threadIdx.x; i < A.stages * Cfg::NCH; i += kThreads) {
+  for (int i = threadIdx.x; i < A.stages * Cfg::NCH; i += Cfg::THREADS) {
     const int stg = i / Cfg::NCH, ch = i % Cfg::NCH;
     uint8_t* cell = smem + L.win + (stg * (A.win_cells + 1) * Cfg::NCH + ch * (A.win_cells + 1) + A.win_cells) * 16;
     uint32_t w[4];
@@ -448,8 +462,8 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
     }
     *reinterpret_cast<uint4*>(cell) = make_uint4(w[0], w[1], w[2], w[3]);
   }
-  for (int i = threadIdx.x; i < Cfg::HD; i += kThreads) s_b1[i] = A.b1[i];
-  for (int i = threadIdx.x; i < Cfg::C; i += kThreads) s_b2[i] = A.b2[i];
+  for (int i = threadIdx.x; i < Cfg::HD; i += Cfg::THREADS) s_b1[i] = A.b1[i];
+  for (int i = threadIdx.x; i < Cfg::C; i += Cfg::THREADS) s_b2[i] = A.b2[i];
   if (warp == 0) {
     tmem_alloc(tmem_holder, Cfg::TMEM_COLS);
     tmem_relinquish();
@@ -460,23 +474,25 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
   const uint32_t tmem = *tmem_holder;
   // A previous launch on this control block failed: do not touch the state.
   const bool skip = (*((volatile int*)&A.ctrl[0]) != 0);
+  const int wg = warp >> 2;
 
   const int grid = gridDim.x;
   const long long total = A.total;
   const int W = A.W;
 
-  if (!skip && warp == 0) {
+  if (!skip && wg == 0) {
+  if (warp == 0) {
     // ---------------------------------------------------------------- MMA issuer
     if (Cfg::TILEDEP && lane == 1 && A.n_steps > 1) {
       // ------------------------------------------------------------ publisher
-      // In tile order: once the 8 epilogue warps have stored tile t of step s, a gpu-scope
+      // In tile order: once the epilogue warps have stored tile t of step s, a gpu-scope
       // fence (cumulative over those stores, acquired at CTA scope) and the tile's counter
       // tile_steps[t] = s + 1, which the loaders of neighbouring tiles wait for.
-      long long it = 0;
+      uint32_t it = 0;
       bool ok = true;
       for (int s = 0; ok && s + 1 < A.n_steps; ++s) {
         for (long long t = blockIdx.x; t < A.n_tiles; t += grid, ++it) {
-          const unsigned want = 8u * (unsigned)(it + 1);
+          const unsigned want = (unsigned)(Cfg::EPI_WARPS + (Cfg::ADAPTIVE ? 2 : 0)) * (unsigned)(it + 1);
           uint64_t start = 0;
           for (uint32_t k = 0;; ++k) {
             unsigned v;
@@ -523,7 +539,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
       const bool wlo = Cfg::SPLIT && A.wimg_lo != nullptr;
       const uint64_t d1lo = umma_desc_sw128(smem_u32(smem + L.w1lo));
       const uint64_t d2lo = umma_desc_sw128(smem_u32(smem + L.w2lo));
-      long long it = 0;
+      uint32_t it = 0;
       for (int s = 0; ok && s < A.n_steps; ++s) {
         for (long long t = blockIdx.x; ok && t < A.n_tiles; t += grid, ++it) {
           const int slot = (int)(it % Cfg::NZ);
@@ -595,7 +611,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
       }
     }
     __syncwarp();
-  } else if (!skip && warp == 1) {
+  } else if (warp == 1) {
     // ---------------------------------------------------------------- loader
     if (lane == 0) {
       const int tot = Cfg::W1_BYTES + Cfg::W2_BYTES;   // w1 and w2 are contiguous in smem
@@ -617,7 +633,9 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
     const int NCH = Cfg::NCH;
     const int WC = A.win_cells;
     const int S = A.stages;
-    long long it = 0;
+    int stage = 0;      // window stage of the current tile: it % S, kept incrementally
+    uint32_t vph = 0;   // (it / S) & 1
+    uint32_t it = 0;
     bool ok = true;
     int done_step = 0;  // every tile has stored the steps before done_step
     for (int s = 0; ok && s < A.n_steps; ++s) {
@@ -645,9 +663,9 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         }
         if (__shfl_sync(0xffffffffu, give_up, 0)) { ok = false; break; }
       }
-      for (long long t = blockIdx.x; t < A.n_tiles; t += grid, ++it) {
-        const int stage = (int)(it % S);
-        const uint32_t v = (uint32_t)(it / S);
+      for (long long t = blockIdx.x; t < A.n_tiles;
+           t += grid, ++it, stage = (stage + 1 == S ? 0 : stage + 1), vph ^= (stage == 0 ? 1u : 0u)) {
+        const uint32_t v = vph;  // parity of the stage's use
         if (!warp_wait(&bars[BAR_WIN_EMPTY + stage], (v & 1) ^ 1, fs, W_LOAD_EMPTY)) { ok = false; break; }
         const long long wb = t * kTileM - W - 1;
         const long long lo = wb < 0 ? 0 : wb;
@@ -694,8 +712,17 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           }
           if (!ok) break;
         }
-        if (lane == 0) mbar_arrive_expect_tx(&bars[BAR_WIN_FULL + stage], (uint32_t)(NCH * (hi - lo) * 16));
+        if (lane == 0)
+          mbar_arrive_expect_tx(&bars[BAR_WIN_FULL + stage],
+                                (uint32_t)(NCH * (hi - lo) * 16) + (Cfg::ADAPTIVE ? kTileM * 4u : 0u));
         __syncwarp();
+        if constexpr (Cfg::ADAPTIVE) {
+          // the fire probabilities of the tile's cells for this step (written by the epilogue at
+          // the previous step, or before the launch)
+          if (lane == 31)
+            bulk_g2s(smem_u32(smem + L.pwin + stage * kTileM * 4), A.fire_p + t * kTileM, kTileM * 4,
+                     &bars[BAR_WIN_FULL + stage]);
+        }
         const uint32_t dst = smem_u32(smem + L.win + stage * (WC + 1) * Cfg::ROWB);
         // one bulk copy per (chunk, tile overlapped by the window): 3 tiles while the board is
         // narrower than a tile, up to 2 + ceil((2W + 2) / 128) for wider boards
@@ -712,13 +739,12 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
                      &bars[BAR_WIN_FULL + stage]);
           }
         }
-        if constexpr (Cfg::HILO && Cfg::ADAPTIVE) {
-          // the tile's lo parts, read by the adaptive rule in the stencil and by E2: into L2
-          // (measured: +4 % adaptive; the same prefetch without the adaptive rule gains nothing)
-          if (lane == 0)
-            bulk_prefetch_l2(reinterpret_cast<const uint8_t*>(A.master[in]) + t * kTileM * Cfg::C * 2,
-                             kTileM * Cfg::C * 2);
-        }
+        // The part of the tile's old state that the epilogue reads from global memory (the lo
+        // parts in the hi/lo layout, else the fp32 state; the adaptive rule reads it too): into
+        // L2 now, a few tiles before the epilogue's loads.
+        if (lane == 0)
+          bulk_prefetch_l2(reinterpret_cast<const uint8_t*>(A.master[in]) + t * kTileM * Cfg::C * (Cfg::HILO ? 2 : 4),
+                           kTileM * Cfg::C * (Cfg::HILO ? 2 : 4));
       }
     }
     // Bulk copies still in flight (only after an abort) must land before the CTA exits.
@@ -733,6 +759,59 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
       }
     }
     __syncwarp();
+  } else if (Cfg::ADAPTIVE) {
+    // ---------------------------------------------------------------- confidence (warps 2, 3)
+    // Adaptive rules: per tile, the readout slices of the new state (copied to shared memory by
+    // the epilogue) -> head_readout -> the cell's fire probability of the next step, 2 rows per
+    // lane.  The stores count for the step end like the epilogue's.
+    const int cw = warp - 2;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int s = 0; ok && s < A.n_steps; ++s) {
+      for (long long t = blockIdx.x; t < A.n_tiles; t += grid, ++it) {
+        const int sl = (int)(it % kSliceSlots);
+        const uint32_t sph = (it / kSliceSlots) & 1;
+        const float* slice = reinterpret_cast<const float*>(smem + L.slice) + sl * kTileM * (A.c_out + 1);
+        if (!warp_wait(&bars[BAR_SLICE_FULL + sl], sph, fs, W_CONF)) { ok = false; break; }
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          const int r = cw * 64 + rr * 32 + lane;
+          const long long g = t * kTileM + r;
+          if (g < total) {
+            const float* row = slice + r * (A.c_out + 1);
+            float xs[16];
+#pragma unroll
+            for (int c = 0; c < 16; ++c) xs[c] = c < A.c_out ? row[c] : 0.f;
+            float conf;
+            int arg;
+            head_readout(A.head_kind, A.n_out, A.c_out, A.head_w, A.head_b, xs, conf, arg);
+            A.fire_p[g] = adaptive_prob(A.fire_mode, conf, row[A.c_out] != 0.f, A.ad_scale, A.ad_bias,
+                                        A.p_low, A.tau, A.p_fire, A.given_confident);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive_relaxed(&bars[BAR_SLICE_EMPTY + sl]);
+        if constexpr (Cfg::TILEDEP) {
+          __syncwarp();
+          if (lane == 0) asm volatile("red.release.cta.shared::cta.add.u32 [%0], 1;" ::"r"(smem_u32(s_tiles_done)) : "memory");
+        }
+      }
+      if constexpr (!Cfg::TILEDEP) {
+        // the step end of the epilogue warps, joined by these two warps (their stores of the step
+        // are then covered by the epilogue's fence before the step counter)
+        unsigned any_fail;
+        asm volatile(
+            "{\n\t.reg .pred p, q;\n\t"
+            "setp.ne.u32 p, %1, 0;\n\t"
+            "bar.red.or.pred q, 1, %2, p;\n\t"
+            "selp.u32 %0, 1, 0, q;\n\t}"
+            : "=r"(any_fail)
+            : "r"((unsigned)(!ok || *(volatile int*)abort_flag != 0)), "n"(Cfg::EPI_WARPS * 32 + 64)
+            : "memory");
+        if (any_fail) { ok = false; break; }
+      }
+    }
+  }  // without the adaptive rules, warps 2 and 3 are idle
   } else if (!skip && warp >= kStencilWarp0 && warp < kEpiWarp0) {
     // ---------------------------------------------------------------- stencil
     const int sw = warp - kStencilWarp0;
@@ -742,18 +821,20 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     const int WC = A.win_cells;
     const int S = A.stages;
-    long long it = 0;
+    int stage = 0;      // window stage of the current tile: it % S, kept incrementally
+    uint32_t vph = 0;   // (it / S) & 1
+    uint32_t it = 0;
     bool ok = true;
     for (int s = 0; ok && s < A.n_steps; ++s) {
-      for (long long t = blockIdx.x; t < A.n_tiles; t += grid, ++it) {
-        const int stage = (int)(it % S);
-        const uint32_t v = (uint32_t)(it / S);
+      for (long long t = blockIdx.x; t < A.n_tiles;
+           t += grid, ++it, stage = (stage + 1 == S ? 0 : stage + 1), vph ^= (stage == 0 ? 1u : 0u)) {
+        const uint32_t v = vph;  // parity of the stage's use
         const int slot = (int)(it % Cfg::NZ);
         const uint32_t u = (uint32_t)(it / Cfg::NZ);
-        if (!warp_wait(&bars[BAR_WIN_FULL + stage], v & 1, fs, W_ST_WINFULL)) { ok = false; break; }
-        if (!warp_wait(&bars[BAR_Z_EMPTY + slot], (u & 1) ^ 1, fs, W_ST_ZEMPTY)) { ok = false; break; }
-        tc_fence_after();
-        const uint8_t* win = smem + L.win + stage * (WC + 1) * Cfg::ROWB;
+        // Index math and the per-row side information for the epilogue come before the waits
+        // (they depend only on the cell and the step, and their global loads then overlap the
+        // wait for the window): bit 0 the fire decision of this step, bit 1 given, bit 2 valid
+        // (the adaptive rules are evaluated after z, below).
         const unsigned g = (unsigned)t * kTileM + m;
         const bool valid = (long long)g < total;
         int i = 0, j = 0, inst = 0, p = 0;
@@ -763,18 +844,30 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           i = (int)fdiv((unsigned)p, A.div_w);
           j = p - i * W;
         }
-        if (!Cfg::ADAPTIVE && half == 0) {
-          // per-row side information for the epilogue: bit 0 the fire decision of this step,
-          // bit 1 given, bit 2 valid (the adaptive rules are evaluated after z, below)
-          uint32_t fl = 0;
-          if (valid) {
-            const int row = A.inst_row ? A.inst_row[inst] : (int)fdiv((unsigned)inst, A.div_k);
-            fl = 4u | (A.given[(long long)row * A.HW + p] ? 2u : 0u);
-            if (A.fire_mode == 0) {
-              fl |= A.masks[((long long)s * A.n_inst + inst) * A.HW + p] ? 1u : 0u;
-            } else {
-              fl |= philox_uniform(A.seed, A.inst_offset + (A.inst_id ? A.inst_id[inst] : inst), p, A.step0 + s) < A.p_fire ? 1u : 0u;
-            }
+        uint32_t fl = 0;
+        float ufire = 0.f;  // adaptive rules: the uniform the cell's fire probability is drawn against
+        if (half == 0 && valid) {
+          const int row = A.inst_row ? A.inst_row[inst] : (int)fdiv((unsigned)inst, A.div_k);
+          fl = 4u | (A.given[(long long)row * A.HW + p] ? 2u : 0u);
+          if constexpr (Cfg::ADAPTIVE) {
+            ufire = (A.fire_mode == 3 || A.fire_mode == 5)
+                        ? A.uniforms[((long long)s * A.n_inst + inst) * A.HW + p]
+                        : philox_uniform(A.seed, A.inst_offset + (A.inst_id ? A.inst_id[inst] : inst), p, A.step0 + s);
+          } else if (A.fire_mode == 0) {
+            fl |= A.masks[((long long)s * A.n_inst + inst) * A.HW + p] ? 1u : 0u;
+          } else {
+            fl |= philox_uniform(A.seed, A.inst_offset + (A.inst_id ? A.inst_id[inst] : inst), p, A.step0 + s) < A.p_fire ? 1u : 0u;
+          }
+        }
+        if (!warp_wait(&bars[BAR_WIN_FULL + stage], v & 1, fs, W_ST_WINFULL)) { ok = false; break; }
+        if (!warp_wait(&bars[BAR_Z_EMPTY + slot], (u & 1) ^ 1, fs, W_ST_ZEMPTY)) { ok = false; break; }
+        tc_fence_after();
+        const uint8_t* win = smem + L.win + stage * (WC + 1) * Cfg::ROWB;
+        if (half == 0) {
+          if constexpr (Cfg::ADAPTIVE) {
+            // the cell's fire probability of this step, copied with the window
+            const float pf = reinterpret_cast<const float*>(smem + L.pwin + stage * kTileM * 4)[m];
+            fl |= (valid && ufire < pf) ? 1u : 0u;
           }
           s_flags[(it & 3) * kTileM + m] = (uint8_t)fl;
           __syncwarp();
@@ -897,27 +990,6 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
             }
           }
         }
-        // Adaptive rules: every stencil warp takes 16 cells of the tile, lanes 0..15, cell ma.
-        // In the hi/lo layout the hi parts of the readout slice are read from the window now,
-        // before z is handed off (the epilogue releases the stage after that).
-        const int ma = quarter * 32 + half * 16 + (lane & 15);
-        const unsigned ga = (unsigned)t * kTileM + ma;
-        const bool va = Cfg::ADAPTIVE && lane < 16 && (long long)ga < total;
-        float xhi[16];
-#pragma unroll
-        for (int c = 0; c < 16; ++c) xhi[c] = 0.f;
-        if constexpr (Cfg::HILO && Cfg::ADAPTIVE) {
-          if (va) {
-            const int ca = ma + W + 1;  // window index of cell ma
-#pragma unroll
-            for (int c = 0; c < 16; ++c)
-              if (c < A.c_out) {
-                const int cc = A.out_off + c;
-                xhi[c] = bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(
-                    win + ((cc >> 3) * (WC + 1) + ca) * 16 + (cc & 7) * 2));
-              }
-          }
-        }
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -925,37 +997,32 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
           mbar_arrive_relaxed(&bars[BAR_Z_FULL + slot]);
           // hi/lo layout: the epilogue still reads the tile's own cells (the hi part of the old
           // state) from this window and releases it
-          if constexpr (!Cfg::HILO) mbar_arrive(&bars[BAR_WIN_EMPTY + stage]);
-        }
-        if constexpr (Cfg::ADAPTIVE) {
-          // adaptive rules: the fire decision needs the confidence of the cell's fp32 state; it
-          // is evaluated after z is handed to the MMA warp (the epilogue needs it a tile later)
-          if (lane < 16) {
-            uint32_t fl = 0;
-            if (va) {
-              const int inst_a = (int)fdiv(ga, A.div_hw);
-              const int p_a = (int)(ga - (unsigned)inst_a * A.HW);
-              const int row = A.inst_row ? A.inst_row[inst_a] : (int)fdiv((unsigned)inst_a, A.div_k);
-              const bool gv = A.given[(long long)row * A.HW + p_a] != 0;
-              fl = 4u | (gv ? 2u : 0u);
-              fl |= adaptive_fire<Cfg>(A, s, t, ma, inst_a, p_a, gv, xhi) ? 1u : 0u;
-            }
-            s_flags[(it & 3) * kTileM + ma] = (uint8_t)fl;
-          }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&bars[BAR_FLAGS + (it & 3)]);
+          if constexpr (!Cfg::HILO) mbar_arrive_relaxed(&bars[BAR_WIN_EMPTY + stage]);
         }
       }
     }
   } else if (!skip && warp >= kEpiWarp0) {
     // ---------------------------------------------------------------- epilogue
+    // Part p of the epilogue (EPI_PARTS warps per lane quarter): E1 of the hidden units
+    // [p * HPART, (p + 1) * HPART), which lie in GEMM1 N-half hh, and E2 of the channels
+    // [p * CH, (p + 1) * CH).
     const int ew = warp - kEpiWarp0;
-    const int half = ew >> 2;
+    const int part = ew >> 2;
+    const int hh = part / Cfg::PARTS_PER_HALF;
+    const int sub = part % Cfg::PARTS_PER_HALF;
     const int quarter = warp & 3;
     const int m = quarter * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    constexpr int CH = Cfg::C / 2;          // channels of this thread in E2
-    long long it = 0;
+    constexpr int CH = Cfg::CH;             // channels of this thread in E2
+    constexpr int HPART = Cfg::HD / Cfg::EPI_PARTS;
+    // columns per tensor-memory load in split mode's E1 (it writes hi and lo parts)
+    constexpr int E1C = 16;
+    // bf16 mode writes h over accumulator columns already read: the second part of a half
+    // writes into the first part's columns, after that part's reads (BAR_PAIR of the lane
+    // quarter and half, one phase per tile)
+    uint64_t* pair_bar = &bars[BAR_PAIR + quarter + 4 * hh];
+    uint32_t it = 0;
+    int wstage = 0;  // window stage of the current tile (it % stages)
     bool ok = true;
     for (int s = 0; ok && s < A.n_steps; ++s) {
       const int in = (A.cur + s) & 1;
@@ -963,7 +1030,8 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
       const float* xin = A.master[in];
       float* xout = A.master[out];
       uint16_t* mout = A.mirror[out];
-      for (long long t = blockIdx.x; t < A.n_tiles; t += grid, ++it) {
+      for (long long t = blockIdx.x; t < A.n_tiles;
+           t += grid, ++it, wstage = (wstage + 1 == A.stages ? 0 : wstage + 1)) {
         const int slot = (int)(it % Cfg::NZ);
         const uint32_t zbase = tmem + lane_addr + slot * Cfg::SLOT_COLS;
         const int rg = (int)(it % Cfg::NACC);             // accumulator region of the tile
@@ -976,71 +1044,114 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         int inst = 0;
         if (valid) inst = (int)fdiv(g, A.div_hw);
         constexpr int NQ = CH / 4;  // float4 chunks of this thread
-        const float4* xin4 = reinterpret_cast<const float4*>(xin) + ((t * (Cfg::C / 4) + half * NQ) << 7) + m;
-        // ---- E1: hidden = relu(acc1 + b1) -> bf16 into the z slot
-        if (!warp_wait(&bars[(half == 0 ? BAR_ACC_FULL : BAR_ACC_FULL_B) + rg], ua, fs, W_E1_ACC)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll 1
-        for (int cbk = 0; cbk < Cfg::HD / 2; cbk += 32) {
-          const int col = half * (Cfg::HD / 2) + cbk;
-          uint32_t r[32];
-          tmem_ld32(abase + col, r);
-          tc_wait_ld_regs(r);
-          const float4* bb = reinterpret_cast<const float4*>(s_b1 + col);
-          uint32_t hi[16];
-          if constexpr (!Cfg::SPLIT) {
+        const float4* xin4 = reinterpret_cast<const float4*>(xin) + ((t * (Cfg::C / 4) + part * NQ) << 7) + m;
+        // The part of the old state that E2 reads from global memory (the lo parts in the hi/lo
+        // layout, else the fp32 state) is requested now, so that its latency overlaps E1.
+        float4 xo[NQ];
+        uint4 lo_pre[Cfg::HILO ? CH / 8 : 1];
+        if constexpr (Cfg::HILO) {
+          const uint4* lo4 = reinterpret_cast<const uint4*>(xin) + ((t * (Cfg::C / 8) + part * (CH / 8)) << 7) + m;
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
+          for (int j = 0; j < CH / 8; ++j) lo_pre[j] = valid ? ld_nc_u4(lo4 + (j << 7)) : make_uint4(0u, 0u, 0u, 0u);
+        } else {
+#pragma unroll
+          for (int q = 0; q < NQ; ++q) xo[q] = valid ? ld_nc_f4(xin4 + (q << 7)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        // ---- E1: hidden = relu(acc1 + b1) -> bf16 (bf16 mode: over the accumulator columns of
+        // the half already read, h of the half at [hh * HD / 2, hh * HD / 2 + HD / 4); split mode:
+        // hi and lo parts into the consumed z slot)
+        if (!warp_wait(&bars[(hh == 0 ? BAR_ACC_FULL : BAR_ACC_FULL_B) + rg], ua, fs, W_E1_ACC)) { ok = false; break; }
+        tc_fence_after();
+        if constexpr (!Cfg::SPLIT) {
+          // bf16 mode: 16-column chunks, the next chunk's tensor-memory load in flight while this
+          // one is converted (tcgen05.wait::ld waits for all of the thread's loads, so one load
+          // is outstanding at a time)
+          constexpr int NCHK = HPART / 16;
+          uint32_t r0[16], r1[16];
+          tmem_ld16(abase + part * HPART, r0);
+#pragma unroll
+          for (int c = 0; c < NCHK; ++c) {
+            uint32_t(&rc)[16] = (c & 1) ? r1 : r0;
+            uint32_t(&rn)[16] = (c & 1) ? r0 : r1;
+            tc_wait_ld_regs(rc);
+            if (c + 1 < NCHK) tmem_ld16(abase + part * HPART + (c + 1) * 16, rn);
+            if (Cfg::PARTS_PER_HALF > 1 && sub == 0 && c == NCHK - 1) {
+              // every column of this part is read: the second part of the half may overwrite them
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive_relaxed(pair_bar);
+            }
+            const float4* bb = reinterpret_cast<const float4*>(s_b1 + part * HPART + c * 16);
+            uint32_t hi[8];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
               const float4 b = bb[q];
-              const float2 h0 = __fadd2_rn(f2(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1])), f2(b.x, b.y));
-              const float2 h1 = __fadd2_rn(f2(__uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])), f2(b.z, b.w));
+              const float2 h0 = __fadd2_rn(f2(__uint_as_float(rc[4 * q]), __uint_as_float(rc[4 * q + 1])), f2(b.x, b.y));
+              const float2 h1 = __fadd2_rn(f2(__uint_as_float(rc[4 * q + 2]), __uint_as_float(rc[4 * q + 3])), f2(b.z, b.w));
               hi[2 * q] = pack_bf16_relu(h0.x, h0.y);
               hi[2 * q + 1] = pack_bf16_relu(h1.x, h1.y);
             }
-            tmem_st16(abase + half * (Cfg::HD / 2) + cbk / 2, hi);  // over the columns already read
-          } else {
-            uint32_t lo[16];
-#pragma unroll
-            for (int q = 0; q < 16; ++q) {
-              const float h0 = fmaxf(__uint_as_float(r[2 * q]) + s_b1[col + 2 * q], 0.f);
-              const float h1 = fmaxf(__uint_as_float(r[2 * q + 1]) + s_b1[col + 2 * q + 1], 0.f);
-              hi[q] = pack_bf16(h0, h1);
-              lo[q] = pack_bf16(h0 - bf16lo_to_f32(hi[q]), h1 - bf16hi_to_f32(hi[q]));
+            if (Cfg::PARTS_PER_HALF > 1 && sub > 0 && c == 0) {
+              if (!warp_wait(pair_bar, (uint32_t)it & 1, fs, W_E1_PAIR)) { ok = false; break; }
+              tc_fence_after();
             }
-            tmem_st16(zbase + col / 2, hi);
-            tmem_st16(zbase + Cfg::HD / 2 + col / 2, lo);
+            tmem_st8(abase + hh * (Cfg::HD / 2) + (sub * HPART + c * 16) / 2, hi);
+          }
+        } else {
+#pragma unroll 1
+        for (int cbk = 0; cbk < HPART; cbk += E1C) {
+          const int col = part * HPART + cbk;
+          uint32_t r[E1C];
+          if constexpr (E1C == 32) tmem_ld32(abase + col, *reinterpret_cast<uint32_t(*)[32]>(r));
+          else tmem_ld16(abase + col, *reinterpret_cast<uint32_t(*)[16]>(r));
+          tc_wait_ld_regs(r);
+          uint32_t hi[E1C / 2];
+          uint32_t lo[E1C / 2];
+#pragma unroll
+          for (int q = 0; q < E1C / 2; ++q) {
+            const float h0 = fmaxf(__uint_as_float(r[2 * q]) + s_b1[col + 2 * q], 0.f);
+            const float h1 = fmaxf(__uint_as_float(r[2 * q + 1]) + s_b1[col + 2 * q + 1], 0.f);
+            hi[q] = pack_bf16(h0, h1);
+            lo[q] = pack_bf16(h0 - bf16lo_to_f32(hi[q]), h1 - bf16hi_to_f32(hi[q]));
+          }
+          if constexpr (E1C == 32) {
+            tmem_st16(zbase + col / 2, *reinterpret_cast<uint32_t(*)[16]>(hi));
+            tmem_st16(zbase + Cfg::HD / 2 + col / 2, *reinterpret_cast<uint32_t(*)[16]>(lo));
+          } else {
+            tmem_st8(zbase + col / 2, *reinterpret_cast<uint32_t(*)[8]>(hi));
+            tmem_st8(zbase + Cfg::HD / 2 + col / 2, *reinterpret_cast<uint32_t(*)[8]>(lo));
           }
         }
+        }
+        if (!ok) break;
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_relaxed(&bars[(half == 0 ? BAR_H_FULL : BAR_H_FULL_B) + rg]);
+        if (lane == 0) mbar_arrive_relaxed(&bars[(hh == 0 ? BAR_H_FULL : BAR_H_FULL_B) + rg]);
 
-        // ---- E2: dx = acc2 + b2; x' = x + f * dx; clamp; store.  The old state of this thread's
-        // channels is loaded while GEMM2 runs.
-        float4 xo[NQ];
+        // ---- E2: dx = acc2 + b2; x' = x + f * dx; clamp; store.
         if constexpr (Cfg::HILO) {
-          // old state = hi, this tile's own cells in the window stage of the stencil, + lo from
-          // global memory
-          const uint4* lo4 = reinterpret_cast<const uint4*>(xin) + ((t * (Cfg::C / 8) + half * (CH / 8)) << 7) + m;
-          const uint8_t* wst = smem + L.win + (int)(it % A.stages) * (A.win_cells + 1) * Cfg::ROWB;
+          // old state = hi, this tile's own cells in the window stage of the stencil, + lo
+          const uint8_t* wst = smem + L.win + wstage * (A.win_cells + 1) * Cfg::ROWB;
 #pragma unroll
           for (int j = 0; j < CH / 8; ++j) {
-            const uint4 lo = valid ? __ldg(lo4 + (j << 7)) : make_uint4(0u, 0u, 0u, 0u);
+            const uint4 lo = lo_pre[j];
             const uint4 hi = *reinterpret_cast<const uint4*>(
-                wst + ((half * (CH / 8) + j) * (A.win_cells + 1) + (m + W + 1)) * 16);
+                wst + ((part * (CH / 8) + j) * (A.win_cells + 1) + (m + W + 1)) * 16);
             xo[2 * j] = make_float4(bf16lo_to_f32(hi.x) + bf16lo_to_f32(lo.x), bf16hi_to_f32(hi.x) + bf16hi_to_f32(lo.x),
                                     bf16lo_to_f32(hi.y) + bf16lo_to_f32(lo.y), bf16hi_to_f32(hi.y) + bf16hi_to_f32(lo.y));
             xo[2 * j + 1] = make_float4(bf16lo_to_f32(hi.z) + bf16lo_to_f32(lo.z), bf16hi_to_f32(hi.z) + bf16hi_to_f32(lo.z),
                                         bf16lo_to_f32(hi.w) + bf16lo_to_f32(lo.w), bf16hi_to_f32(hi.w) + bf16hi_to_f32(lo.w));
           }
-          // the stencil warps finished every read of this window before handing z to the MMA
-          // warp, and this warp has its hi values: release the stage to the loader
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&bars[BAR_WIN_EMPTY + (int)(it % A.stages)]);
-        } else {
+          // The stencil warps finished every read of this window before handing z to the MMA
+          // warp, and this warp has used its hi values (the empty asm below takes the sums as
+          // inputs, so the instructions that consume the shared-memory loads come before it):
+          // release the stage to the loader.  The arrive is relaxed: a release arrive would first
+          // wait for this thread's global stores of the previous tile.
 #pragma unroll
-          for (int q = 0; q < NQ; ++q) xo[q] = valid ? __ldg(xin4 + (q << 7)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int q = 0; q < NQ; ++q) asm volatile("" ::"f"(xo[q].x), "f"(xo[q].y), "f"(xo[q].z), "f"(xo[q].w));
+          __syncwarp();
+          if (lane == 0) mbar_arrive_relaxed(&bars[BAR_WIN_EMPTY + wstage]);
         }
         if (!warp_wait(&bars[BAR_FLAGS + (it & 3)], (uint32_t)(it >> 2) & 1, fs, W_E2_FLAGS)) { ok = false; break; }
 
@@ -1051,41 +1162,56 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
         tc_fence_after();
         uint32_t r[CH];
         if constexpr (CH == 32) {
-          tmem_ld32(abase + (Cfg::ACC2_COL - Cfg::ACC_COL) + half * CH, r);
+          tmem_ld32(abase + (Cfg::ACC2_COL - Cfg::ACC_COL) + part * CH, r);
         } else if constexpr (CH == 16) {
-          tmem_ld16(abase + (Cfg::ACC2_COL - Cfg::ACC_COL) + half * CH, *reinterpret_cast<uint32_t(*)[16]>(r));
+          tmem_ld16(abase + (Cfg::ACC2_COL - Cfg::ACC_COL) + part * CH, *reinterpret_cast<uint32_t(*)[16]>(r));
         } else {
           static_assert(CH == 8, "channels per epilogue thread");
-          tmem_ld8(abase + (Cfg::ACC2_COL - Cfg::ACC_COL) + half * CH, *reinterpret_cast<uint32_t(*)[8]>(r));
+          tmem_ld8(abase + (Cfg::ACC2_COL - Cfg::ACC_COL) + part * CH, *reinterpret_cast<uint32_t(*)[8]>(r));
         }
         tc_wait_ld_regs(r);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_relaxed(&bars[BAR_ACC_EMPTY + rg]);
+        // Adaptive rules: the part that holds the readout slice writes it to shared memory once the
+        // confidence warps have read the previous tile's.
+        const bool slice_here = Cfg::ADAPTIVE && part == A.out_off / CH;
+        if constexpr (Cfg::ADAPTIVE) {
+          if (slice_here && !warp_wait(&bars[BAR_SLICE_EMPTY + (int)(it % kSliceSlots)],
+                                       ((it / kSliceSlots) & 1) ^ 1, fs, W_CONF)) { ok = false; break; }
+        }
         if (valid) {
-          const float4* bb = reinterpret_cast<const float4*>(s_b2 + half * CH);
+          const float4* bb = reinterpret_cast<const float4*>(s_b2 + part * CH);
           const float2 ff = f2(f, f);
-          float4* xout4 = reinterpret_cast<float4*>(xout) + ((t * (Cfg::C / 4) + half * NQ) << 7) + m;
+          float4* xout4 = reinterpret_cast<float4*>(xout) + ((t * (Cfg::C / 4) + part * NQ) << 7) + m;
           // Clamp (src/nca/model.py:430-438) of the input slice of given cells.  The state this
           // kernel reads is clamped already (the initial state is, every step keeps it so, and
           // the host follows the first step on an unclamped state with a clamp pass), so the old
           // values of those channels are kept: a select per channel, no branch, no reads of the
           // clamp rows.
-          const int lo_c = A.in_off - half * CH;  // input slice relative to this thread's channels
+          const int lo_c = A.in_off - part * CH;  // input slice relative to this thread's channels
           const unsigned long long slice = A.c_in >= 64 ? ~0ull : ((1ull << A.c_in) - 1ull);
           const uint32_t keep = (gv && lo_c < CH && lo_c + A.c_in > 0)
                                     ? (uint32_t)((slice << (lo_c + 32)) >> 32)
                                     : 0u;
           // the bf16 mirror of each 8 channels is stored as soon as they are done (fewer live
           // registers than packing all of them first)
-          uint4* mout4 = reinterpret_cast<uint4*>(mout) + ((t * (Cfg::C / 8) + half * (CH / 8)) << 7) + m;
-          uint4* lout4 = reinterpret_cast<uint4*>(xout) + ((t * (Cfg::C / 8) + half * (CH / 8)) << 7) + m;
+          uint4* mout4 = reinterpret_cast<uint4*>(mout) + ((t * (Cfg::C / 8) + part * (CH / 8)) << 7) + m;
+          uint4* lout4 = reinterpret_cast<uint4*>(xout) + ((t * (Cfg::C / 8) + part * (CH / 8)) << 7) + m;
           uint32_t pk[4], pl[4];
           // Test-time noise (src/nca/perturb.py:23-40): added after the update, before the clamp
           // (src/nca/model.py:544-546); only the NOISE instantiation carries this code.
           bool nz = false;
           int p_cell = 0;
           long long nid = 0;
+          // Adaptive rules: the part that holds the readout slice copies the values it stores for
+          // those channels (and the given flag) to the row's slice in shared memory; the
+          // confidence warps compute the cell's fire probability of the next step from them.
+          float* s_slice = reinterpret_cast<float*>(smem + L.slice) +
+                           ((int)(it % kSliceSlots) * kTileM + m) * (A.c_out + 1);
+          if constexpr (Cfg::ADAPTIVE) {
+            if (slice_here) s_slice[A.c_out] = gv ? 1.f : 0.f;
+          }
           if constexpr (Cfg::NOISE) {
             p_cell = (int)(g - (unsigned)inst * A.HW);
             nid = A.inst_offset + (A.inst_id ? A.inst_id[inst] : inst);
@@ -1108,7 +1234,7 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
             if constexpr (Cfg::NOISE) {
               if (nz) {
                 float4 e;
-                const int c0 = half * CH + 4 * q;  // first channel of this chunk
+                const int c0 = part * CH + 4 * q;  // first channel of this chunk
                 if (A.noise_mode == 1) {
                   const float4 z = normal4(philox_tagged(A.seed, 3u, nid, (uint32_t)(p_cell * (Cfg::C / 4) + (c0 >> 2)),
                                                          A.step0 + s));
@@ -1135,6 +1261,12 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
               pk[2 * (q & 1) + 1] = h1;
               pl[2 * (q & 1)] = pack_bf16(y0.x - bf16lo_to_f32(h0), y0.y - bf16hi_to_f32(h0));
               pl[2 * (q & 1) + 1] = pack_bf16(y1.x - bf16lo_to_f32(h1), y1.y - bf16hi_to_f32(h1));
+              if (Cfg::ADAPTIVE && slice_here) {
+                // the stored state hi + lo of these 4 channels
+                const uint32_t l0 = pl[2 * (q & 1)], l1 = pl[2 * (q & 1) + 1];
+                y0 = f2(bf16lo_to_f32(h0) + bf16lo_to_f32(l0), bf16hi_to_f32(h0) + bf16hi_to_f32(l0));
+                y1 = f2(bf16lo_to_f32(h1) + bf16lo_to_f32(l1), bf16hi_to_f32(h1) + bf16hi_to_f32(l1));
+              }
               if (q & 1) {
                 mout4[(q >> 1) << 7] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 lout4[(q >> 1) << 7] = make_uint4(pl[0], pl[1], pl[2], pl[3]);
@@ -1147,9 +1279,24 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
                 if (q & 1) mout4[(q >> 1) << 7] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
               }
             }
+            if constexpr (Cfg::ADAPTIVE) {
+              if (slice_here) {
+                const int cb = part * CH + 4 * q - A.out_off;  // slice index of the chunk's channel 0
+                const float vv[4] = {y0.x, y0.y, y1.x, y1.y};
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  if (cb + e >= 0 && cb + e < A.c_out) s_slice[cb + e] = vv[e];
+              }
+            }
           }
         }
-        if (half == 0 && A.updates != nullptr) {
+        if constexpr (Cfg::ADAPTIVE) {
+          if (slice_here) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars[BAR_SLICE_FULL + (int)(it % kSliceSlots)]);
+          }
+        }
+        if (part == 0 && A.updates != nullptr) {
           const bool fired = valid && f > 0.f;
           const unsigned grp = __match_any_sync(0xffffffffu, valid ? inst : -1);
           const unsigned fm = __ballot_sync(0xffffffffu, fired);
@@ -1167,15 +1314,16 @@ __global__ void __launch_bounds__(kThreads, 1) nca_step_kernel(const __grid_cons
       }
       if constexpr (!Cfg::TILEDEP) {
         // Step done: this CTA's stores of step s are complete.  The barrier also ORs the failure
-        // flags of the 8 epilogue warps so that they leave the step loop together.
+        // flags of the epilogue warps so that they leave the step loop together.
         unsigned any_fail;
         asm volatile(
             "{\n\t.reg .pred p, q;\n\t"
             "setp.ne.u32 p, %1, 0;\n\t"
-            "bar.red.or.pred q, 1, 256, p;\n\t"
+            "bar.red.or.pred q, 1, %2, p;\n\t"
             "selp.u32 %0, 1, 0, q;\n\t}"
             : "=r"(any_fail)
-            : "r"((unsigned)(!ok || *(volatile int*)abort_flag != 0))
+            : "r"((unsigned)(!ok || *(volatile int*)abort_flag != 0)),
+              "n"(Cfg::EPI_WARPS * 32 + (Cfg::ADAPTIVE ? 64 : 0))
             : "memory");
         if (any_fail) { ok = false; break; }
         if (threadIdx.x == kEpiWarp0 * 32) {

@@ -3,8 +3,10 @@
 `B200Engine` takes any model object with the reference's layout (nca.model.NCA or
 ncas_b200.model.NCA): `cfg`, `perceive.weight`, `update.fc1/fc2`, `head`.  It packs the MLP
 weights once into the bf16 shared-memory image the tcgen05 kernels read, and exposes the
-operations of the rollout path on device tensors.  All compute is done by the library; torch
-provides device memory, the current CUDA stream and host<->device copies.
+operations of the rollout path on device tensors.  All compute is done by the library, called
+through its torch operators (torch.ops.nca_b200.*, ncas_b200._ops) on torch's current CUDA
+stream; torch provides device memory, the stream and host<->device copies.  Host-side size
+queries and the weight packing call the C ABI directly (ctypes).
 
 `B200RolloutBlocks` is the drop-in for nca.engine.inference.UniformRolloutBlocks
 (src/nca/engine/inference.py:79-104): same constructor shape and `__call__(x, given4, clamp,
@@ -21,6 +23,7 @@ import numpy as np
 import torch
 
 from . import _lib as L
+from ._ops import as_bytes, ops
 from .model import FIXED_TAPS, check_supported
 
 # Limit of any single wait inside a kernel (a grid barrier, a pipeline handoff).
@@ -82,6 +85,7 @@ class State:
             "nca_b200_state_bind",
         )
         self.n_inst, self.hw = n_inst, hw
+        self.bytes = as_bytes(self.st)  # the struct as the operators take it
 
 
 class B200Engine:
@@ -160,6 +164,7 @@ class B200Engine:
         d.b1 = self.b1.data_ptr()
         d.b2 = self.b2.data_ptr()
         self.desc = d
+        self.desc_bytes = as_bytes(d)
         self.embed = model.embed.detach().float().to(self.device) if hasattr(model, "embed") else None
         self.ctrl = torch.zeros(4, dtype=torch.int32, device=self.device)
         self.timeout_ms = DEFAULT_TIMEOUT_MS
@@ -194,7 +199,9 @@ class B200Engine:
         d.given, d.clamp, d.inputs = g.data_ptr(), c.data_ptr(), x.data_ptr()
         d.inst_row = _ptr(ir)
         d.inst_id = _ptr(iid)
-        return Batch(d, n, H, W, trials, g, c, x, ir, iid)
+        b = Batch(d, n, H, W, trials, g, c, x, ir, iid)
+        b.bytes = as_bytes(d)
+        return b
 
     def compacted(self, b: Batch, sel: torch.Tensor) -> Batch:
         """The batch of the instances `sel` (increasing) of b: same board rows and Philox trial
@@ -227,22 +234,19 @@ class B200Engine:
         return _stream(self.device)
 
     def init_state(self, st: State, b: Batch) -> None:
-        L.check(L.lib().nca_b200_state_init(C.byref(st.st), C.byref(self.desc), C.byref(b.desc), self._s()),
-                "nca_b200_state_init")
+        ops().state_init(st.bytes, self.desc_bytes, b.bytes)
         self.launches += 1
 
     def load_nchw(self, st: State, x: torch.Tensor) -> None:
         x = x.to(self.device, torch.float32).contiguous()
-        L.check(L.lib().nca_b200_state_load_nchw(C.byref(st.st), x.data_ptr(), self._s()),
-                "nca_b200_state_load_nchw")
+        ops().load_nchw(st.bytes, x)
         self.launches += 1
 
     def store_nchw(self, st: State, out: torch.Tensor | None = None) -> torch.Tensor:
         H_W = st.hw
         if out is None:
             out = torch.empty((st.n_inst, self.channels, H_W), dtype=torch.float32, device=self.device)
-        L.check(L.lib().nca_b200_state_store_nchw(C.byref(st.st), out.data_ptr(), self._s()),
-                "nca_b200_state_store_nchw")
+        ops().store_nchw(st.bytes, out)
         self.launches += 1
         return out
 
@@ -304,22 +308,16 @@ class B200Engine:
                 f.noise_p_t, f.noise_p_s = float(noise["p_t"]), float(noise["p_s"])
                 f.noise_sigma = float(noise["sigma"])
                 f.noise_until = int(noise["until"])
-        L.check(
-            L.lib().nca_b200_run_steps(
-                C.byref(self.desc), C.byref(b.desc), C.byref(st.st), int(n_steps), C.byref(f),
-                self.ctrl.data_ptr(), int(self.timeout_ms), self._s()
-            ),
-            "nca_b200_run_steps",
-        )
+        ops().run_steps(self.desc_bytes, b.bytes, st.bytes, int(n_steps), as_bytes(f), self.ctrl,
+                        int(self.timeout_ms))
         self.launches += 1  # the step kernel (the control-word reset is a memset)
         self._keep = keep  # alive until the next call (the kernel reads them asynchronously)
 
     def check(self) -> None:
         """Synchronise and raise if a kernel reported a failure in the control words."""
-        detail = C.c_int32(0)
-        s = L.lib().nca_b200_ctrl_status(self.ctrl.data_ptr(), C.byref(detail), self._s())
+        s, detail = ops().ctrl_status(self.ctrl)
         if s != L.NCA_OK:
-            raise L.NcaError(s, "kernel", detail.value)
+            raise L.NcaError(s, "kernel", detail)
 
     # ------------------------------------------------------------------ readout and selection
     def readout(self, st: State, b: Batch, targets: torch.Tensor | None = None,
@@ -336,14 +334,8 @@ class B200Engine:
             tg = targets.to(dev, torch.uint8).reshape(-1, hw).contiguous()
             out["cell_acc"] = torch.empty(n, dtype=torch.float32, device=dev)
             out["exact"] = torch.empty(n, dtype=torch.uint8, device=dev)
-        L.check(
-            L.lib().nca_b200_readout(
-                C.byref(self.desc), C.byref(b.desc), C.byref(st.st), _ptr(out.get("pred")),
-                _ptr(out.get("cell_conf")), out["board_conf"].data_ptr(), _ptr(tg),
-                _ptr(out.get("cell_acc")), _ptr(out.get("exact")), self._s()
-            ),
-            "nca_b200_readout",
-        )
+        ops().readout(self.desc_bytes, b.bytes, st.bytes, out.get("pred"), out.get("cell_conf"),
+                      out["board_conf"], tg, out.get("cell_acc"), out.get("exact"))
         self.launches += 1
         return out
 
@@ -354,13 +346,8 @@ class B200Engine:
         best = torch.empty(n_boards, dtype=torch.float32, device=dev)
         bp = torch.empty((n_boards, hw), dtype=torch.uint8, device=dev) if pred is not None else None
         al = None if alive is None else alive.to(dev, torch.uint8).contiguous()
-        L.check(
-            L.lib().nca_b200_select(
-                board_conf.data_ptr(), _ptr(al), n_boards, trials, int(k_limit or trials),
-                idx.data_ptr(), best.data_ptr(), _ptr(pred), hw, _ptr(bp), self._s()
-            ),
-            "nca_b200_select",
-        )
+        ops().select(board_conf.contiguous(), al, n_boards, trials, int(k_limit or trials), idx, best,
+                     None if pred is None else pred.contiguous(), hw, bp)
         self.launches += 1
         return idx, best, bp
 
@@ -369,14 +356,9 @@ class B200Engine:
         dev = self.device
         src = torch.empty(n_boards * trials, dtype=torch.int32, device=dev)
         kept = torch.empty(n_boards * trials, dtype=torch.uint8, device=dev)
-        L.check(
-            L.lib().nca_b200_prune_refill(
-                pred.data_ptr(), board_conf.data_ptr(), n_boards, trials, pred.shape[-1], int(n_cap),
-                src.data_ptr(), kept.data_ptr(), self._s()
-            ),
-            "nca_b200_prune_refill",
-        )
-        L.check(L.lib().nca_b200_clone(C.byref(st.st), src.data_ptr(), self._s()), "nca_b200_clone")
+        ops().prune_refill(pred.contiguous(), board_conf.contiguous(), n_boards, trials, pred.shape[-1],
+                           int(n_cap), src, kept)
+        ops().clone(st.bytes, src)
         self.launches += 2
         return src, kept
 
@@ -384,8 +366,7 @@ class B200Engine:
         """Damage event: zero state in the cells of masks (rows, H*W) (one mask per board row),
         clamp re-applied (src/nca/rollout.py:206-212)."""
         mk = masks.to(self.device, torch.uint8).contiguous()
-        L.check(L.lib().nca_b200_damage(C.byref(self.desc), C.byref(b.desc), C.byref(st.st),
-                                        mk.data_ptr(), self._s()), "nca_b200_damage")
+        ops().damage(self.desc_bytes, b.bytes, st.bytes, mk)
         self._keep_damage = mk
         self.launches += 1
 
@@ -409,13 +390,8 @@ class B200Engine:
         rank = torch.empty(rows, dtype=torch.int32, device=dev)
         n_niches = torch.empty(n, dtype=torch.int32, device=dev)
         hw = int(pred.shape[-1])
-        L.check(
-            L.lib().nca_b200_niches(
-                pred.data_ptr(), board_conf.data_ptr(), row_start.data_ptr(), n, max_rows, hw,
-                niche.data_ptr(), rank.data_ptr(), n_niches.data_ptr(), self._s()
-            ),
-            "nca_b200_niches",
-        )
+        ops().niches(pred.contiguous(), board_conf.contiguous(), row_start, n, max_rows, hw, niche, rank,
+                     n_niches)
         nn = n_niches.cpu().numpy()
         order = np.zeros(max(1, int(nn.sum())), dtype=np.int32)
         order_start = np.zeros(n, dtype=np.int32)
@@ -430,14 +406,8 @@ class B200Engine:
         keep = torch.empty(rows, dtype=torch.uint8, device=dev)
         order_d = torch.from_numpy(order).to(dev)
         order_start_d = torch.from_numpy(order_start).to(dev)
-        L.check(
-            L.lib().nca_b200_halving(
-                niche.data_ptr(), rank.data_ptr(), n_niches.data_ptr(), row_start.data_ptr(),
-                order_d.data_ptr(), order_start_d.data_ptr(), n, max_rows, int(n_cap),
-                keep.data_ptr(), self._s()
-            ),
-            "nca_b200_halving",
-        )
+        ops().halving(niche, rank, n_niches, row_start, order_d, order_start_d, n, max_rows, int(n_cap),
+                      keep)
         self.launches += 2
         return keep
 
@@ -445,8 +415,7 @@ class B200Engine:
         """A new state holding the instances `sel` of st (compaction)."""
         sel32 = sel.to(self.device, torch.int32).contiguous()
         dst = self.new_state(int(sel32.numel()), st.hw)
-        L.check(L.lib().nca_b200_gather(C.byref(st.st), C.byref(dst.st), sel32.data_ptr(), self._s()),
-                "nca_b200_gather")
+        ops().gather(st.bytes, dst.bytes, sel32)
         self.launches += 1
         return dst
 

@@ -51,6 +51,7 @@ import numpy as np
 import torch
 
 from . import _lib as L
+from ._ops import ops
 from .engine import B200Engine
 from .perturb import circular_masks, sample_noise
 from .tasks import Boards, Task
@@ -362,9 +363,7 @@ def select_best(conf: np.ndarray, alive: np.ndarray, k: int, device=None) -> np.
     a = torch.from_numpy(np.ascontiguousarray(alive, dtype=np.uint8)).to(dev)
     idx = torch.empty(N, dtype=torch.int32, device=dev)
     best = torch.empty(N, dtype=torch.float32, device=dev)
-    stream = torch.cuda.current_stream(dev).cuda_stream
-    L.check(L.lib().nca_b200_select(c.data_ptr(), a.data_ptr(), N, K, int(min(k, K)), idx.data_ptr(),
-                                    best.data_ptr(), None, 0, None, stream), "nca_b200_select")
+    ops().select(c, a, N, K, int(min(k, K)), idx, best, None, 0, None)
     return idx.cpu().numpy().astype(np.int64)
 
 

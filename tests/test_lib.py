@@ -76,9 +76,10 @@ def test_state_bytes(lib):
     lo = tiles * 128 * 64 * 2  # bf16 mode: hi (mirror) and lo bf16 arrays, two buffers each
     hi = tiles * 128 * 64 * 2
     flags = (tiles * 4 + 255) & ~255  # per-tile step counters
-    assert n.value == 2 * lo + 2 * hi + flags
+    fire_p = tiles * 128 * 4  # per-cell fire probabilities of the confidence rules
+    assert n.value == 2 * lo + 2 * hi + flags + fire_p
     assert lib.nca_b200_state_bytes(10, 81, 64, L.PREC_SPLIT, C.byref(n)) == 0
-    assert n.value == 2 * (-(-810 // 128) * 128 * 64 * 4 + 255 & ~255) + 256
+    assert n.value == 2 * (-(-810 // 128) * 128 * 64 * 4 + 255 & ~255) + 256 + 7 * 128 * 4
     assert lib.nca_b200_state_bytes(0, 81, 64, 0, C.byref(n)) == 1
 
 
@@ -111,3 +112,31 @@ def test_no_cuda_means_a_loud_error():
     m = build_model("maze", device="cpu")
     with pytest.raises(RuntimeError, match="CUDA"):
         m.engine()
+
+
+def test_torch_operators_are_registered_with_their_schemas(lib):
+    """The operator library loads without a GPU and registers every rollout entry point of the C
+    ABI as torch.ops.nca_b200.* (the engine calls them)."""
+    from ncas_b200._ops import as_bytes, ops
+
+    o = ops()
+    want = {
+        "state_init": "nca_b200::state_init(Tensor state, Tensor model, Tensor batch) -> ()",
+        "run_steps": "nca_b200::run_steps(Tensor model, Tensor batch, Tensor state, int n_steps, "
+                     "Tensor fire, Tensor(a!) ctrl, int timeout_ms) -> ()",
+        "select": "nca_b200::select(Tensor board_conf, Tensor? alive, int n_boards, int trials, "
+                  "int k_limit, Tensor(a!) best_idx, Tensor(b!) best_conf, Tensor? pred, int hw, "
+                  "Tensor(c!)? best_pred) -> ()",
+        "ctrl_status": "nca_b200::ctrl_status(Tensor(a!) ctrl) -> int[]",
+    }
+    for name, schema in want.items():
+        assert str(getattr(o, name).default._schema) == schema
+    for name in ("load_nchw", "store_nchw", "readout", "prune_refill", "clone", "damage", "niches",
+                 "halving", "gather"):
+        assert hasattr(o, name)
+    # a descriptor is a view of the ctypes struct's bytes
+    st = L.NcaState()
+    v = as_bytes(st)
+    assert v.dtype.itemsize == 1 and v.numel() == C.sizeof(L.NcaState)
+    v[0] = 7
+    assert st.n_inst == 7

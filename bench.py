@@ -286,7 +286,8 @@ def run_ours(args) -> None:
                 ev1 = torch.cuda.Event(enable_timing=True)
                 ev0.record()
                 eng.run(st, batch, b - a, mode="adaptive" if adaptive else "philox", p_fire=bc.p_fire,
-                        seed=0, step0=a, updates=updates, adaptive=adaptive or (0.9, 0.1))
+                        seed=0, step0=a, updates=updates, adaptive=adaptive or (0.9, 0.1),
+                        resident=not args.no_resident)
                 ev1.record()
                 if timed:
                     kern.append((ev0, ev1))
@@ -327,7 +328,7 @@ def run_ours(args) -> None:
     task = task_for(bc)
     rc = RolloutConfig(depth=bc.depth, k=K, fire_rate=bc.p_fire, max_cells=1 << 40,
                        pruning={"every": bc.prune_every, "n_cap": bc.n_cap} if bc.prune_every else None,
-                       engine={"fire": "philox", "precision": args.precision,
+                       engine={"fire": "philox", "precision": args.precision, "resident": not args.no_resident,
                                **({"adaptive": {"scale": 0.9, "bias": 0.1}} if bc.adaptive else {})})
     if not args.no_e2e:
         e2e_steps = max(1, min(args.steps, 3))
@@ -362,6 +363,7 @@ def run_ours(args) -> None:
             "data": "synthetic",
             "config": {"workload": bc.name, "boards": n_total, "boards_per_gpu": n, "k": K,
                        "depth": bc.depth, "hw": HW, "task": bc.task, "precision": args.precision,
+                       "resident": not args.no_resident,
                        "parallelism": f"{n_total} boards over {world} GPU(s), all K trials of a board on one GPU",
                        "l2": f"state {state_bytes / 1e9:.2f} GB per GPU vs 126 MB L2"},
             "roofline": roofline(bc, args.precision, kdur, kcells),
@@ -392,6 +394,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the public-API (host buffers) pass")
     ap.add_argument("--no-split", action="store_true", help="skip the split-precision measurement")
+    ap.add_argument("--no-resident", action="store_true",
+                    help="stream every step through HBM (no shared-memory-resident kernel)")
     ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
                     help="strong: the workload's boards split over the GPUs; weak: every GPU runs them")
     ap.add_argument("--boards", type=int, default=None, help="smaller case of the workload (profiling)")

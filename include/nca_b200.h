@@ -151,6 +151,12 @@ typedef struct NcaFireDesc {
   int64_t noise_until;
   const float* noise;       /* NCA_NOISE_EXTERNAL: device [n_inst][C][H*W] noise of the single
                                step of the call (n_steps must be 1) */
+  int32_t resident;         /* 1: run the steps with each instance's state resident in shared
+                               memory when whole instances fit (bf16 precision, fewer than 64
+                               channels, no noise or confidence rules, n_steps > 1): the state is
+                               kept as bf16 hi + lo parts between the steps of the call and read
+                               from / written to HBM once; 0 (or when it does not apply): the
+                               streaming kernel, one HBM round trip per step */
 } NcaFireDesc;
 
 /* ---- library / device --------------------------------------------------------------------- */

@@ -110,6 +110,7 @@ class NcaFireDesc(C.Structure):
         ("noise_sigma", C.c_float),
         ("noise_until", C.c_int64),
         ("noise", C.c_void_p),
+        ("resident", C.c_int32),
     ]
 
 

@@ -79,30 +79,53 @@ inline int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaSta
   A.ctrl = ctrl;
   A.timeout_ns = (unsigned long long)(timeout_ms > 0 ? timeout_ms : 10000) * 1000000ull;
 
-  // Window stages: in the hi/lo layout a window lives from the stencil to the epilogue (which
-  // reads the hi part of the old state from it), so more stages keep the stencil ahead.
-  int stages = Cfg::HILO ? kMaxStages : 2;
-  int smem = SmemLayout<Cfg>(stages, A.win_cells, A.wimg_lo != nullptr, A.c_out).total + 1024;
-  while (smem > kMaxSmem && stages > 1) {
-    --stages;
-    smem = SmemLayout<Cfg>(stages, A.win_cells, A.wimg_lo != nullptr, A.c_out).total + 1024;
-  }
-  if (smem > kMaxSmem) return NCA_ERR_UNSUPPORTED;
-  A.stages = stages;
-
   int dev = 0, sms = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return NCA_ERR_CUDA;
   e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return NCA_ERR_CUDA;
-  const long long grid_ll = A.n_tiles < sms ? A.n_tiles : sms;
+
+  int stages, smem;
+  long long grid_ll;
+  if constexpr (Cfg::RESIDENT) {
+    // Groups of whole instances: as many as fit the shared memory (the two hi buffers and the lo
+    // parts), but no more than spread the batch over every SM.
+    if (n_steps < 2 || A.total + 2LL * kTileM >= (1LL << 31)) return NCA_ERR_UNSUPPORTED;
+    auto smem_for = [&](long long inst) {
+      return SmemLayout<Cfg>(2, (int)(inst * A.HW), false, A.c_out).total + 1024LL;
+    };
+    long long g_cap = 0;
+    while (smem_for(g_cap + 1) <= kMaxSmem && g_cap < A.n_inst) ++g_cap;
+    if (g_cap < 1) return NCA_ERR_UNSUPPORTED;
+    const long long spread = (A.n_inst + sms - 1) / sms;
+    const long long g = g_cap < spread ? g_cap : spread;
+    A.res_inst = (int)g;
+    A.res_cells = g * A.HW;
+    A.n_groups = (A.n_inst + g - 1) / g;
+    stages = 2;
+    A.win_cells = (int)A.res_cells;  // the padding cell follows the group's cells
+    smem = (int)smem_for(g);
+    grid_ll = A.n_groups < sms ? A.n_groups : sms;
+  } else {
+    // Window stages: in the hi/lo layout a window lives from the stencil to the epilogue (which
+    // reads the hi part of the old state from it), so more stages keep the stencil ahead.
+    stages = Cfg::HILO ? kMaxStages : 2;
+    smem = SmemLayout<Cfg>(stages, A.win_cells, A.wimg_lo != nullptr, A.c_out).total + 1024;
+    while (smem > kMaxSmem && stages > 1) {
+      --stages;
+      smem = SmemLayout<Cfg>(stages, A.win_cells, A.wimg_lo != nullptr, A.c_out).total + 1024;
+    }
+    if (smem > kMaxSmem) return NCA_ERR_UNSUPPORTED;
+    grid_ll = A.n_tiles < sms ? A.n_tiles : sms;
+  }
+  A.stages = stages;
   const int grid = (int)(grid_ll > 0 ? grid_ll : 1);
   // Steps are ordered by per-tile step counters when every CTA has few tiles (a grid barrier
   // would idle the whole GPU at each step boundary), else by the grid barrier on ctrl[2], whose
   // cost is then small against the step (the per-tile form costs the epilogue registers and the
   // MMA warp a publisher lane).
-  const bool tiledep = n_steps > 1 && A.n_tiles <= (long long)kTileDepPerCta * grid;
-  using CfgTD = StepCfg<Cfg::C, Cfg::HD, Cfg::SPLIT, Cfg::NOISE, true, Cfg::ADAPTIVE>;
+  const bool tiledep = !Cfg::RESIDENT && n_steps > 1 && A.n_tiles <= (long long)kTileDepPerCta * grid;
+  using CfgTD = StepCfg<Cfg::C, Cfg::HD, Cfg::SPLIT, Cfg::NOISE, !Cfg::RESIDENT, Cfg::ADAPTIVE, Cfg::RESIDENT>;
   auto kern = tiledep ? nca_step_kernel<CfgTD> : nca_step_kernel<Cfg>;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return NCA_ERR_CUDA;
@@ -115,7 +138,7 @@ inline int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaSta
   }
   e = cudaMemsetAsync(ctrl + 2, 0, sizeof(int32_t), stream);
   if (e != cudaSuccess) return NCA_ERR_CUDA;
-  if (n_steps > 1) {
+  if (n_steps > 1 && !Cfg::RESIDENT) {  // the resident kernel's CTAs never wait for each other
     void* args[] = {&A};
     e = cudaLaunchCooperativeKernel((const void*)kern, dim3(grid), dim3(Cfg::THREADS), args,
                                     (size_t)smem, stream);

@@ -49,13 +49,18 @@ __host__ __device__ constexpr int epi_part_channels(int C) { return C / 2; }
 __host__ __device__ constexpr bool hilo_layout(int C, bool bf16) { return bf16 && C >= 64; }
 
 template <int C_, int HD_, bool SPLIT_, bool NOISE_ = false, bool TILEDEP_ = false,
-          bool ADAPTIVE_ = false>
+          bool ADAPTIVE_ = false, bool RESIDENT_ = false>
 struct StepCfg {
   static constexpr int C = C_;
   static constexpr bool NOISE = NOISE_;  // test-time state noise (a separate instantiation)
   // fire decisions on the cell's confidence (fire modes 2..5): the epilogue computes each cell's
   // fire probability for the next step from the values it stores, the stencil draws against it
   static constexpr bool ADAPTIVE = ADAPTIVE_;
+  // Shared-memory-resident mode: each CTA takes groups of whole instances and keeps their state
+  // in shared memory for all steps of the launch (bf16 hi parts in two buffers that alternate
+  // between steps -- the stencil's source --, lo parts in place); no grid barrier, HBM is read
+  // at a group's start and written at its last step.  bf16 mode below 64 channels.
+  static constexpr bool RESIDENT = RESIDENT_;
   // steps ordered by per-tile step counters (StepArgs::tile_steps) instead of a grid barrier
   static constexpr bool TILEDEP = TILEDEP_;
   static constexpr int P = 4 * C_;
@@ -100,6 +105,9 @@ struct StepCfg {
   static_assert(NCH % 2 == 0, "stencil channel halves");
   static_assert(!H_IN_ACC || C <= HD / 4, "acc2 must fit next to h in the accumulator region");
   static_assert(NUM_WARPS % 4 == 0 && CH % 8 == 0, "warp groups and E2 channel shares");
+  static_assert(EPI_WARPS <= 8, "progress words of the resident mode");
+  static_assert(!RESIDENT || (!SPLIT && !HILO && !NOISE && !ADAPTIVE && !TILEDEP),
+                "the resident mode is a bf16-mode kernel without noise or confidence rules");
 };
 
 // n / d for 0 <= n < 2^31 with a multiply-high and a shift (Granlund & Montgomery, "Division by
@@ -126,6 +134,9 @@ struct StepArgs {
   int n_steps;
   long long step0;
   int stages, win_cells;
+  // resident mode: instances per group, cells per group (res_inst * HW), groups
+  int res_inst;
+  long long res_cells, n_groups;
   float pad[64];  // state of the cells outside a board (zero padding: 0), by channel
   int c_in, in_off, c_out, out_off, n_out, fixed_taps;
   float taps[4][9];
@@ -166,7 +177,7 @@ constexpr int kSliceSlots = 1;  // adaptive rules: readout-slice buffers between
 // Shared-memory layout (offsets from a 1024-byte aligned base).
 template <class Cfg>
 struct SmemLayout {
-  int w1, w2, w1lo, w2lo, win, pwin, slice, b1, b2, flags, bars, misc, total;
+  int w1, w2, w1lo, w2lo, win, rlo, pwin, slice, b1, b2, flags, bars, misc, total;
   // c_out: readout channels (the adaptive rules keep each row's readout slice here)
   __host__ __device__ SmemLayout(int stages, int win_cells, bool lo, int c_out) {
     w1 = 0;
@@ -174,7 +185,10 @@ struct SmemLayout {
     w1lo = w2 + Cfg::W2_BYTES;  // the residual image, when present, follows (same layout)
     w2lo = w1lo + Cfg::W1_BYTES;
     win = ((lo ? w2lo + Cfg::W2_BYTES : w1lo) + 1023) & ~1023;
-    pwin = (win + stages * (win_cells + 1) * Cfg::ROWB + 15) & ~15;  // + the padding cell
+    rlo = (win + stages * (win_cells + 1) * Cfg::ROWB + 15) & ~15;  // + the padding cell
+    // resident mode: the window stages are the two buffers of the hi parts of the group's state
+    // (win_cells = cells of a group) and the lo parts follow, [chunk][cell][16 B]
+    pwin = rlo + (Cfg::RESIDENT ? win_cells * Cfg::ROWB : 0);
     // adaptive rules: the tile's fire probabilities, one fp32 per row, with each window stage,
     // and the epilogue's copy of each row's new readout slice (c_out fp32 per row)
     slice = pwin + (Cfg::ADAPTIVE ? stages * kTileM * 4 : 0);
@@ -186,6 +200,37 @@ struct SmemLayout {
     total = misc + 64;
   }
 };
+
+// The tiles of one CTA, as one or more passes.  Streaming: one pass, tiles t = blockIdx.x +
+// k * grid of the whole batch at every step.  Resident: one pass per group of instances
+// (groups blockIdx.x + k * grid), tiles 0 .. T - 1 of the group at every step.  The global cell
+// of row m of tile t is cell0 + t * 128 + m; rows at or past `lim` are not cells.
+struct Pass {
+  long long t0, t1, dt, cell0, lim;
+};
+template <class Cfg>
+__device__ __forceinline__ long long pass_count(const StepArgs& A, int grid) {
+  if constexpr (Cfg::RESIDENT) return (A.n_groups - blockIdx.x + grid - 1) / grid;
+  return 1;
+}
+template <class Cfg>
+__device__ __forceinline__ Pass pass_of(const StepArgs& A, long long ps, int grid) {
+  Pass P;
+  if constexpr (Cfg::RESIDENT) {
+    P.cell0 = (blockIdx.x + ps * grid) * A.res_cells;
+    P.lim = P.cell0 + A.res_cells < A.total ? P.cell0 + A.res_cells : A.total;
+    P.t0 = 0;
+    P.t1 = (P.lim - P.cell0 + kTileM - 1) / kTileM;
+    P.dt = 1;
+  } else {
+    P.cell0 = 0;
+    P.lim = A.total;
+    P.t0 = blockIdx.x;
+    P.t1 = A.n_tiles;
+    P.dt = grid;
+  }
+  return P;
+}
 
 constexpr int kMaxStages = 4;  // window stages
 #ifndef NCA_TILEDEP_PER_CTA
@@ -213,14 +258,15 @@ enum BarId {
   BAR_PAIR = 30,
   BAR_SLICE_FULL = 38,   // +slot (2): adaptive rules, the epilogue has written a tile's readout slices
   BAR_SLICE_EMPTY = 40,  // +slot (2): the confidence warps have read them
-  BAR_COUNT = 42
+  BAR_RES_LOADED = 42,   // resident mode: the epilogue warps have loaded a group's state
+  BAR_COUNT = 43
 };
 static_assert(BAR_COUNT <= kBarSlots, "barrier area of the shared-memory layout");
 
 // Failure sites reported in ctrl[1].
 enum Where {
   W_MMA_ZFULL = 1, W_MMA_ACCEMPTY, W_MMA_HFULL, W_MMA_WEIGHTS, W_LOAD_EMPTY, W_LOAD_GRID,
-  W_ST_WINFULL, W_ST_ZEMPTY, W_E1_ACC, W_E2_ACC2, W_DRAIN, W_E2_FLAGS, W_PUBLISH, W_E1_PAIR, W_CONF
+  W_ST_WINFULL, W_ST_ZEMPTY, W_E1_ACC, W_E2_ACC2, W_DRAIN, W_E2_FLAGS, W_PUBLISH, W_E1_PAIR, W_CONF, W_RES
 };
 
 // A window stage is laid out [chunk][window cell][16 B]: lanes that read the same chunk of
@@ -246,6 +292,35 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const 
     }
     if (__shfl_sync(0xffffffffu, give_up, 0)) return false;
     if (it > 128) __nanosleep(32);
+  }
+}
+
+// Warp-converged bounded wait until each of the n progress words in shared memory is >= need
+// (resident mode: the epilogue warps' count of finished tiles).
+__device__ __forceinline__ bool wait_progress(const unsigned* words, int n, unsigned need,
+                                              const FailState& fs, int where) {
+  const int lane = threadIdx.x & 31;
+  uint64_t start = 0;
+  for (uint32_t it = 0;; ++it) {
+    bool done = true;
+    if (lane < n) {
+      unsigned v;
+      asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(words + lane)) : "memory");
+      done = v >= need;
+    }
+    if (__all_sync(0xffffffffu, done)) return true;
+    int give_up = 0;
+    if (lane == 0 && (it & 63) == 63) {
+      const uint64_t now = global_timer_ns();
+      if (start == 0) start = now;
+      if (should_abort(fs)) give_up = 1;
+      else if (now - start > fs.timeout_ns || it > (1u << 28)) {
+        report_failure(fs, 4, where);
+        give_up = 1;
+      }
+    }
+    if (__shfl_sync(0xffffffffu, give_up, 0)) return false;
+    __nanosleep(32);
   }
 }
 
@@ -329,6 +404,9 @@ __device__ __forceinline__ void state_put(float* master, uint16_t* mirror, int C
 // (copy_head on the host, the callers' slices), so every row sums all 16 channels without a check
 // per channel: the extra terms are exact zeros and leave each score as the sum over c < c_out in
 // increasing order.  Only the rows o < n_out are evaluated.
+// MAXC: a compile-time bound on c_out (the channels past c_out are zeros, see above); the callers
+// on the hot path pick the smallest of 4, 9, 16 that holds c_out (head_readout_auto).
+template <int MAXC = 16>
 __device__ __forceinline__ void head_readout(int kind, int n_out, int c_out, const float (&hw)[16][16],
                                              const float (&hb)[16], const float (&xs)[16],
                                              float& conf, int& arg) {
@@ -344,7 +422,7 @@ __device__ __forceinline__ void head_readout(int kind, int n_out, int c_out, con
       if (kind == 1) {
         float d2 = 0.f;
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
+        for (int c = 0; c < MAXC; ++c) {
           const float d = xs[c] - hw[o][c];
           d2 = fmaf(d, d, d2);
         }
@@ -352,7 +430,7 @@ __device__ __forceinline__ void head_readout(int kind, int n_out, int c_out, con
       } else {
         v = hb[o];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) v = fmaf(hw[o][c], xs[c], v);
+        for (int c = 0; c < MAXC; ++c) v = fmaf(hw[o][c], xs[c], v);
       }
       sc[o] = v;
       if (v > best || o == 0) { best = v; a = o; }
@@ -368,6 +446,14 @@ __device__ __forceinline__ void head_readout(int kind, int n_out, int c_out, con
   for (int o = 0; o < 16; ++o)
     if (o < n_out) den += expf(sc[o] - best);
   conf = fminf(fmaxf(1.f / den, 0.f), 1.f);
+}
+
+__device__ __forceinline__ void head_readout_auto(int kind, int n_out, int c_out, const float (&hw)[16][16],
+                                                  const float (&hb)[16], const float (&xs)[16],
+                                                  float& conf, int& arg) {
+  if (c_out <= 4) head_readout<4>(kind, n_out, c_out, hw, hb, xs, conf, arg);
+  else if (c_out <= 9) head_readout<9>(kind, n_out, c_out, hw, hb, xs, conf, arg);
+  else head_readout<16>(kind, n_out, c_out, hw, hb, xs, conf, arg);
 }
 
 // The head weights of a model as the kernels read them: head_w / head_b zero outside
@@ -440,6 +526,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
     // the flags of a tile come from the 4 half-0 stencil warps
     for (int r = 0; r < 4; ++r) mbar_init(&bars[BAR_FLAGS + r], 4);
     for (int r = 0; r < 8; ++r) mbar_init(&bars[BAR_PAIR + r], 1);
+    mbar_init(&bars[BAR_RES_LOADED], Cfg::EPI_WARPS);
+    for (int i = 0; i < 8; ++i) reinterpret_cast<unsigned*>(smem + L.misc + 32)[i] = 0u;
     for (int r = 0; r < kSliceSlots; ++r) {
       mbar_init(&bars[BAR_SLICE_FULL + r], 4);   // the 4 epilogue warps of the part holding the slice
       mbar_init(&bars[BAR_SLICE_EMPTY + r], 2);  // the 2 confidence warps
@@ -540,8 +628,11 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
       const uint64_t d1lo = umma_desc_sw128(smem_u32(smem + L.w1lo));
       const uint64_t d2lo = umma_desc_sw128(smem_u32(smem + L.w2lo));
       uint32_t it = 0;
+      const long long n_pass = pass_count<Cfg>(A, grid);
+      for (long long ps = 0; ok && ps < n_pass; ++ps) {
+      const Pass P = pass_of<Cfg>(A, ps, grid);
       for (int s = 0; ok && s < A.n_steps; ++s) {
-        for (long long t = blockIdx.x; ok && t < A.n_tiles; t += grid, ++it) {
+        for (long long t = P.t0; ok && t < P.t1; t += P.dt, ++it) {
           const int slot = (int)(it % Cfg::NZ);
           const uint32_t u = (uint32_t)(it / Cfg::NZ);
           const uint32_t zcol = tmem + slot * Cfg::SLOT_COLS;
@@ -602,6 +693,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
           if (!Cfg::H_IN_ACC) umma_commit(&bars[BAR_Z_EMPTY + slot]);
         }
       }
+      }  // passes
       // Drain: every MMA issued above has completed once this commit arrives.
       umma_commit(&bars[BAR_DRAIN]);
       uint64_t t0 = global_timer_ns();
@@ -638,7 +730,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
     uint32_t it = 0;
     bool ok = true;
     int done_step = 0;  // every tile has stored the steps before done_step
-    for (int s = 0; ok && s < A.n_steps; ++s) {
+    // (resident mode: no windows; the epilogue warps load each group's state)
+    for (int s = 0; ok && !Cfg::RESIDENT && s < A.n_steps; ++s) {
       const int in = (A.cur + s) & 1;
       const uint8_t* src = Cfg::SRC_BF16 ? reinterpret_cast<const uint8_t*>(A.mirror[in])
                                          : reinterpret_cast<const uint8_t*>(A.master[in]);
@@ -784,7 +877,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
             for (int c = 0; c < 16; ++c) xs[c] = c < A.c_out ? row[c] : 0.f;
             float conf;
             int arg;
-            head_readout(A.head_kind, A.n_out, A.c_out, A.head_w, A.head_b, xs, conf, arg);
+            head_readout_auto(A.head_kind, A.n_out, A.c_out, A.head_w, A.head_b, xs, conf, arg);
             A.fire_p[g] = adaptive_prob(A.fire_mode, conf, row[A.c_out] != 0.f, A.ad_scale, A.ad_bias,
                                         A.p_low, A.tau, A.p_fire, A.given_confident);
           }
@@ -825,9 +918,13 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
     uint32_t vph = 0;   // (it / S) & 1
     uint32_t it = 0;
     bool ok = true;
+    const long long n_pass = pass_count<Cfg>(A, grid);
+    const unsigned* s_prog = reinterpret_cast<const unsigned*>(smem + L.misc + 32);
+    for (long long ps = 0; ok && ps < n_pass; ++ps) {
+    const Pass P = pass_of<Cfg>(A, ps, grid);
     for (int s = 0; ok && s < A.n_steps; ++s) {
-      for (long long t = blockIdx.x; t < A.n_tiles;
-           t += grid, ++it, stage = (stage + 1 == S ? 0 : stage + 1), vph ^= (stage == 0 ? 1u : 0u)) {
+      for (long long t = P.t0; t < P.t1;
+           t += P.dt, ++it, stage = (stage + 1 == S ? 0 : stage + 1), vph ^= (stage == 0 ? 1u : 0u)) {
         const uint32_t v = vph;  // parity of the stage's use
         const int slot = (int)(it % Cfg::NZ);
         const uint32_t u = (uint32_t)(it / Cfg::NZ);
@@ -835,8 +932,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
         // (they depend only on the cell and the step, and their global loads then overlap the
         // wait for the window): bit 0 the fire decision of this step, bit 1 given, bit 2 valid
         // (the adaptive rules are evaluated after z, below).
-        const unsigned g = (unsigned)t * kTileM + m;
-        const bool valid = (long long)g < total;
+        const unsigned g = (unsigned)(P.cell0 + t * kTileM) + m;
+        const bool valid = (long long)g < P.lim;
         int i = 0, j = 0, inst = 0, p = 0;
         if (valid) {
           inst = (int)fdiv(g, A.div_hw);
@@ -859,10 +956,23 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
             fl |= philox_uniform(A.seed, A.inst_offset + (A.inst_id ? A.inst_id[inst] : inst), p, A.step0 + s) < A.p_fire ? 1u : 0u;
           }
         }
-        if (!warp_wait(&bars[BAR_WIN_FULL + stage], v & 1, fs, W_ST_WINFULL)) { ok = false; break; }
+        if constexpr (Cfg::RESIDENT) {
+          // The hi parts of step s are in buffer s & 1: at the group's first step the epilogue's
+          // load of the group; later the previous step's epilogue of this tile and its
+          // neighbours (up to tile t + 1), which every epilogue warp reports in its progress word.
+          if (s == 0) {
+            if (t == 0 && !warp_wait(&bars[BAR_RES_LOADED], (uint32_t)ps & 1, fs, W_RES)) { ok = false; break; }
+          } else {
+            const long long tn = t + 1 < P.t1 ? t + 1 : P.t1 - 1;
+            const unsigned need = it - (unsigned)(t + P.t1) + (unsigned)tn + 1u;  // it of (s-1, tn), + 1
+            if (!wait_progress(s_prog, Cfg::EPI_WARPS, need, fs, W_RES)) { ok = false; break; }
+          }
+        } else {
+          if (!warp_wait(&bars[BAR_WIN_FULL + stage], v & 1, fs, W_ST_WINFULL)) { ok = false; break; }
+        }
         if (!warp_wait(&bars[BAR_Z_EMPTY + slot], (u & 1) ^ 1, fs, W_ST_ZEMPTY)) { ok = false; break; }
         tc_fence_after();
-        const uint8_t* win = smem + L.win + stage * (WC + 1) * Cfg::ROWB;
+        const uint8_t* win = smem + L.win + (Cfg::RESIDENT ? (s & 1) : stage) * (WC + 1) * Cfg::ROWB;
         if (half == 0) {
           if constexpr (Cfg::ADAPTIVE) {
             // the cell's fire probability of this step, copied with the window
@@ -875,7 +985,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
         }
         const bool up = valid && i > 0, dn = valid && i < A.H - 1;
         const bool lf = valid && j > 0, rt = valid && j < W - 1;
-        const int c0 = m + W + 1;  // window index of this cell
+        // window index of this cell (resident: its index in the group)
+        const int c0 = Cfg::RESIDENT ? (int)(t * kTileM) + m : m + W + 1;
         const uint32_t zbase = tmem + lane_addr + slot * Cfg::SLOT_COLS;
         // the 9 neighbours a b c / d e f / g h k: their cell offsets in the window stage
         const uint32_t wbase = smem_u32(win);
@@ -997,10 +1108,11 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
           mbar_arrive_relaxed(&bars[BAR_Z_FULL + slot]);
           // hi/lo layout: the epilogue still reads the tile's own cells (the hi part of the old
           // state) from this window and releases it
-          if constexpr (!Cfg::HILO) mbar_arrive_relaxed(&bars[BAR_WIN_EMPTY + stage]);
+          if constexpr (!Cfg::HILO && !Cfg::RESIDENT) mbar_arrive_relaxed(&bars[BAR_WIN_EMPTY + stage]);
         }
       }
     }
+    }  // passes
   } else if (!skip && warp >= kEpiWarp0) {
     // ---------------------------------------------------------------- epilogue
     // Part p of the epilogue (EPI_PARTS warps per lane quarter): E1 of the hidden units
@@ -1024,14 +1136,43 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
     uint32_t it = 0;
     int wstage = 0;  // window stage of the current tile (it % stages)
     bool ok = true;
+    const long long n_pass = pass_count<Cfg>(A, grid);
+    unsigned* s_prog = reinterpret_cast<unsigned*>(smem + L.misc + 32);  // resident: per-warp progress
+    for (long long ps = 0; ok && ps < n_pass; ++ps) {
+    const Pass P = pass_of<Cfg>(A, ps, grid);
+    if constexpr (Cfg::RESIDENT) {
+      // The group's state into shared memory (hi parts to buffer 0, lo parts).  Every epilogue
+      // warp is done with the previous group (the barrier at the end of each pass), and the
+      // stencil finished with it before the epilogue's last tile.
+      const int ncells = (int)(P.lim - P.cell0);
+      const int WC = A.win_cells;
+      const float4* x4 = reinterpret_cast<const float4*>(A.master[A.cur & 1]);
+      for (int job = ew * 32 + lane; job < ncells * (Cfg::C / 8); job += Cfg::EPI_WARPS * 32) {
+        const int k = job / ncells, c = job - k * ncells;  // 8-channel chunk, cell of the group
+        const long long gg = P.cell0 + c;
+        const float4* src = x4 + (((gg >> 7) * (Cfg::C / 4) + 2 * k) << 7) + (gg & 127);
+        const float4 a = src[0], b = src[128];
+        const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        uint32_t h[4], l[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          h[e] = pack_bf16(v[2 * e], v[2 * e + 1]);
+          l[e] = pack_bf16(v[2 * e] - bf16lo_to_f32(h[e]), v[2 * e + 1] - bf16hi_to_f32(h[e]));
+        }
+        *reinterpret_cast<uint4*>(smem + L.win + (k * (WC + 1) + c) * 16) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4*>(smem + L.rlo + (k * WC + c) * 16) = make_uint4(l[0], l[1], l[2], l[3]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[BAR_RES_LOADED]);
+    }
     for (int s = 0; ok && s < A.n_steps; ++s) {
       const int in = (A.cur + s) & 1;
       const int out = in ^ 1;
       const float* xin = A.master[in];
       float* xout = A.master[out];
       uint16_t* mout = A.mirror[out];
-      for (long long t = blockIdx.x; t < A.n_tiles;
-           t += grid, ++it, wstage = (wstage + 1 == A.stages ? 0 : wstage + 1)) {
+      for (long long t = P.t0; t < P.t1;
+           t += P.dt, ++it, wstage = (wstage + 1 == A.stages ? 0 : wstage + 1)) {
         const int slot = (int)(it % Cfg::NZ);
         const uint32_t zbase = tmem + lane_addr + slot * Cfg::SLOT_COLS;
         const int rg = (int)(it % Cfg::NACC);             // accumulator region of the tile
@@ -1039,8 +1180,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
         const uint32_t abase = tmem + lane_addr + Cfg::ACC_COL + rg * Cfg::HD;
         // ---- before E1: index math; the fire and given flags come from the stencil warps
         // (s_flags).
-        const unsigned g = (unsigned)t * kTileM + m;
-        const bool valid = (long long)g < total;
+        const unsigned g = (unsigned)(P.cell0 + t * kTileM) + m;
+        const bool valid = (long long)g < P.lim;
         int inst = 0;
         if (valid) inst = (int)fdiv(g, A.div_hw);
         constexpr int NQ = CH / 4;  // float4 chunks of this thread
@@ -1053,7 +1194,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
           const uint4* lo4 = reinterpret_cast<const uint4*>(xin) + ((t * (Cfg::C / 8) + part * (CH / 8)) << 7) + m;
 #pragma unroll
           for (int j = 0; j < CH / 8; ++j) lo_pre[j] = valid ? ld_nc_u4(lo4 + (j << 7)) : make_uint4(0u, 0u, 0u, 0u);
-        } else {
+        } else if constexpr (!Cfg::RESIDENT) {
 #pragma unroll
           for (int q = 0; q < NQ; ++q) xo[q] = valid ? ld_nc_f4(xin4 + (q << 7)) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
@@ -1130,7 +1271,24 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
         if (lane == 0) mbar_arrive_relaxed(&bars[(hh == 0 ? BAR_H_FULL : BAR_H_FULL_B) + rg]);
 
         // ---- E2: dx = acc2 + b2; x' = x + f * dx; clamp; store.
-        if constexpr (Cfg::HILO) {
+        const int cl = (int)(t * kTileM) + m;  // resident: the cell's index in its group
+        if constexpr (Cfg::RESIDENT) {
+          // old state = hi (buffer s & 1) + lo of this thread's channels, in shared memory
+          const int WC = A.win_cells;
+#pragma unroll
+          for (int j = 0; j < CH / 8; ++j) {
+            const int k = part * (CH / 8) + j;
+            uint4 hi = make_uint4(0u, 0u, 0u, 0u), lo = make_uint4(0u, 0u, 0u, 0u);
+            if (valid) {
+              hi = *reinterpret_cast<const uint4*>(smem + L.win + ((s & 1) * (WC + 1) * Cfg::NCH + k * (WC + 1) + cl) * 16);
+              lo = *reinterpret_cast<const uint4*>(smem + L.rlo + (k * WC + cl) * 16);
+            }
+            xo[2 * j] = make_float4(bf16lo_to_f32(hi.x) + bf16lo_to_f32(lo.x), bf16hi_to_f32(hi.x) + bf16hi_to_f32(lo.x),
+                                    bf16lo_to_f32(hi.y) + bf16lo_to_f32(lo.y), bf16hi_to_f32(hi.y) + bf16hi_to_f32(lo.y));
+            xo[2 * j + 1] = make_float4(bf16lo_to_f32(hi.z) + bf16lo_to_f32(lo.z), bf16hi_to_f32(hi.z) + bf16hi_to_f32(lo.z),
+                                        bf16lo_to_f32(hi.w) + bf16lo_to_f32(lo.w), bf16hi_to_f32(hi.w) + bf16hi_to_f32(lo.w));
+          }
+        } else if constexpr (Cfg::HILO) {
           // old state = hi, this tile's own cells in the window stage of the stencil, + lo
           const uint8_t* wst = smem + L.win + wstage * (A.win_cells + 1) * Cfg::ROWB;
 #pragma unroll
@@ -1254,7 +1412,33 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
             y0.y = (keep >> (4 * q + 1)) & 1u ? xo[q].y : y0.y;
             y1.x = (keep >> (4 * q + 2)) & 1u ? xo[q].z : y1.x;
             y1.y = (keep >> (4 * q + 3)) & 1u ? xo[q].w : y1.y;
-            if constexpr (Cfg::HILO) {
+            if constexpr (Cfg::RESIDENT) {
+              if (s + 1 < A.n_steps) {
+                // hi to the other buffer (the stencil's source at the next step), lo in place
+                const uint32_t h0 = pack_bf16(y0.x, y0.y), h1 = pack_bf16(y1.x, y1.y);
+                pk[2 * (q & 1)] = h0;
+                pk[2 * (q & 1) + 1] = h1;
+                pl[2 * (q & 1)] = pack_bf16(y0.x - bf16lo_to_f32(h0), y0.y - bf16hi_to_f32(h0));
+                pl[2 * (q & 1) + 1] = pack_bf16(y1.x - bf16lo_to_f32(h1), y1.y - bf16hi_to_f32(h1));
+                if (q & 1) {
+                  const int k = part * (CH / 8) + (q >> 1);
+                  const int WC = A.win_cells;
+                  *reinterpret_cast<uint4*>(smem + L.win + (((s + 1) & 1) * (WC + 1) * Cfg::NCH + k * (WC + 1) + cl) * 16) =
+                      make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                  *reinterpret_cast<uint4*>(smem + L.rlo + (k * WC + cl) * 16) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+                }
+              } else {
+                // the group's last step: the fp32 state and its bf16 copy to global memory
+                const long long gt = (long long)(g >> 7), gr = g & 127;
+                reinterpret_cast<float4*>(xout)[((gt * (Cfg::C / 4) + part * NQ + q) << 7) + gr] =
+                    make_float4(y0.x, y0.y, y1.x, y1.y);
+                pk[2 * (q & 1)] = pack_bf16(y0.x, y0.y);
+                pk[2 * (q & 1) + 1] = pack_bf16(y1.x, y1.y);
+                if (q & 1)
+                  reinterpret_cast<uint4*>(mout)[((gt * (Cfg::C / 8) + part * (CH / 8) + (q >> 1)) << 7) + gr] =
+                      make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              }
+            } else if constexpr (Cfg::HILO) {
               // hi = bf16(y) to the mirror, lo = bf16(y - hi) to the low array
               const uint32_t h0 = pack_bf16(y0.x, y0.y), h1 = pack_bf16(y1.x, y1.y);
               pk[2 * (q & 1)] = h0;
@@ -1305,6 +1489,13 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
             if (cnt) atomicAdd(&A.updates[inst], (unsigned)cnt);
           }
         }
+        if constexpr (Cfg::RESIDENT) {
+          // this warp is done with the tile (its shared-memory stores are ordered before the
+          // release): the stencil's wait for the next step reads it
+          __syncwarp();
+          if (lane == 0)
+            asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(s_prog + ew)), "r"(it + 1u) : "memory");
+        }
         if constexpr (Cfg::TILEDEP) {
           // this warp's stores of the tile are issued: count it for the publisher lane (the warp
           // barrier orders the lanes' stores before lane 0's release)
@@ -1312,7 +1503,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
           if (lane == 0) asm volatile("red.release.cta.shared::cta.add.u32 [%0], 1;" ::"r"(smem_u32(s_tiles_done)) : "memory");
         }
       }
-      if constexpr (!Cfg::TILEDEP) {
+      if constexpr (!Cfg::TILEDEP && !Cfg::RESIDENT) {
         // Step done: this CTA's stores of step s are complete.  The barrier also ORs the failure
         // flags of the epilogue warps so that they leave the step loop together.
         unsigned any_fail;
@@ -1332,6 +1523,21 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
         }
       }
     }
+    if constexpr (Cfg::RESIDENT) {
+      // End of a group: every epilogue warp is done with it (the next group's load overwrites
+      // its state).  The barrier also ORs the warps' failure flags so that they leave together.
+      unsigned any_fail;
+      asm volatile(
+          "{\n\t.reg .pred p, q;\n\t"
+          "setp.ne.u32 p, %1, 0;\n\t"
+          "bar.red.or.pred q, 2, %2, p;\n\t"
+          "selp.u32 %0, 1, 0, q;\n\t}"
+          : "=r"(any_fail)
+          : "r"((unsigned)(!ok || *(volatile int*)abort_flag != 0)), "n"(Cfg::EPI_WARPS * 32)
+          : "memory");
+      if (any_fail) { ok = false; break; }
+    }
+    }  // passes
   }
 
   __syncthreads();

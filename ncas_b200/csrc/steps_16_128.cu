@@ -12,6 +12,11 @@ int32_t launch_shape_16_128(bool split, bool noise, bool adaptive, const NcaMode
 #define NCA_AD(SP, NZ)                                                                            \
   return adaptive ? launch_steps<StepCfg<16, 128, SP, NZ, false, true>>(m, b, st, n, f, ctrl, timeout_ms, s) \
                   : launch_steps<StepCfg<16, 128, SP, NZ>>(m, b, st, n, f, ctrl, timeout_ms, s);
+  if (!split && !noise && !adaptive && f->resident && n > 1) {
+    // the shared-memory-resident kernel, when a group of instances fits
+    const int32_t r = launch_steps<StepCfg<16, 128, false, false, false, false, true>>(m, b, st, n, f, ctrl, timeout_ms, s);
+    if (r != NCA_ERR_UNSUPPORTED) return r;
+  }
   if (noise) {
     if (split) { NCA_AD(true, true) }
     NCA_AD(false, true)

@@ -266,13 +266,17 @@ class B200Engine:
         updates: torch.Tensor | None = None,
         noise: dict | None = None,
         threshold: tuple[float, float, bool] | None = None,
+        resident: bool = False,
     ) -> None:
         """n_steps NCA steps.  mode: 'mask' (masks (n_steps, n_inst, H*W) uint8), 'philox',
         'adaptive' (Philox, p = a * (1 - conf) + b) or 'adaptive_uniform' (uniforms given);
         'threshold' / 'threshold_uniform': the reference's rule with threshold = (p_low, tau,
         given_confident) (p_low for cells with conf > tau, p_fire for the others).
         noise (test-time state noise): {'p_t', 'p_s', 'sigma', 'until'} drawn in the kernel
-        from Philox, or {'tensor': (n_inst, C, H*W) fp32} for a single step."""
+        from Philox, or {'tensor': (n_inst, C, H*W) fp32} for a single step.
+        resident: keep each instance's state in shared memory for all n_steps when whole
+        instances fit (bf16 mode below 64 channels without noise or confidence rules; the state
+        is kept as bf16 hi + lo parts between the steps), else the streaming kernel."""
         f = L.NcaFireDesc()
         f.mode = {"mask": L.FIRE_MASK, "philox": L.FIRE_PHILOX, "adaptive": L.FIRE_ADAPTIVE_PHILOX,
                   "adaptive_uniform": L.FIRE_ADAPTIVE_UNIFORM, "threshold": L.FIRE_THRESHOLD_PHILOX,
@@ -283,6 +287,7 @@ class B200Engine:
         f.adapt_scale, f.adapt_bias = float(adaptive[0]), float(adaptive[1])
         f.seed = int(seed) & ((1 << 64) - 1)
         f.step0 = int(step0)
+        f.resident = int(bool(resident))
         keep = []
         if masks is not None:
             m = masks.to(self.device, torch.uint8).contiguous()

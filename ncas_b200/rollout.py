@@ -27,6 +27,9 @@ The reference's options on this path:
       on the host from numpy.random.default_rng(seed), the state update is a kernel.
 
 Rules beyond the reference's:
+  resident states: RolloutConfig.engine["resident"] (default True) runs the steps between two
+      observation points with every instance's state in shared memory where whole instances fit
+      (bf16 mode below 64 channels, without noise or confidence rules);
   adaptive firing (continuous):  RolloutConfig.engine["adaptive"] = {"scale": a, "bias": b}
       p_cell = a * (1 - conf_cell) + b with conf_cell = NCA.confidence of the current state;
   niche-capped pruning with refill: RolloutConfig.pruning = {"every": s, "n_cap": c}
@@ -158,6 +161,8 @@ def rollout(model, task: Task, boards: Boards, rc, seed: int = 0, task_ids=None,
     if fire not in ("philox", "torch"):
         raise ValueError("engine['fire'] must be 'philox' or 'torch'")
     adaptive = opts.get("adaptive")
+    # states resident in shared memory between observation points where whole instances fit
+    resident = bool(opts.get("resident", True))
     thr = (float(rc.p_low), float(rc.tau), bool(rc.given_confident)) if rc.p_low is not None else None
     p_fire = cfg.fire_rate if rc.fire_rate is None else rc.fire_rate
     noise = rc.noise
@@ -245,7 +250,7 @@ def rollout(model, task: Task, boards: Boards, rc, seed: int = 0, task_ids=None,
         for bnd in boundaries:
             n_steps = bnd - t
             Bc = int(idx.numel())
-            kw = dict(seed=seed, updates=updates, p_fire=p_fire)
+            kw = dict(seed=seed, updates=updates, p_fire=p_fire, resident=resident)
             if adaptive is not None:
                 kw["adaptive"] = (float(adaptive.get("scale", 0.9)), float(adaptive.get("bias", 0.1)))
             if thr is not None:

@@ -123,3 +123,25 @@ def test_rollout_halving_halves_alive_trials_per_checkpoint():
     # one checkpoint: floor(8 / 2) survivors per board (n_cap large enough to never bind)
     assert np.array_equal(alive.sum(axis=1), [4, 4, 4])
     assert out["decoded"].shape == (24, 9, 9) and np.all(out["updates"] > 0)
+
+
+def test_torch_cpu_port_matches_numpy_oracle():
+    """oracle/torch_cpu.py (the CPU baseline, computed with the reference's torch operators)
+    steps exactly like the numpy oracle on the same masks, maze and sudoku."""
+    import torch
+
+    import oracle.torch_cpu as TC
+    from ncas_b200.configs import model_config, synthetic_params
+    from ncas_b200.tasks import maze_boards, sudoku_boards
+
+    for task, boards in (("maze", maze_boards(2, 19, seed=4)), ("sudoku", sudoku_boards(3, seed=4))):
+        cfg = model_config(task)
+        p = O.params_from_arrays(synthetic_params(cfg, 0), cfg)
+        m = TC.TorchCpuNca(p, cfg.channels)
+        x, g4, cl = TC.init_state(boards.inputs, boards.given, 2, cfg.channels, m.c_in, m.in_off)
+        for t in range(3):
+            fire = (torch.rand((x.shape[0], 1, *x.shape[2:]), generator=torch.Generator().manual_seed(t)) < 0.5).float()
+            want = O.step(x.numpy(), g4.numpy(), cl.numpy(), fire.numpy(), p)
+            with torch.no_grad():
+                x = m.step(x, g4, cl, fire)
+            np.testing.assert_allclose(x.numpy(), want, rtol=1e-5, atol=1e-6)

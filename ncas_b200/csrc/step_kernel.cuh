@@ -1164,6 +1164,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[BAR_RES_LOADED]);
+      // E2 reads cells that other epilogue warps loaded: wait for (acquire) the whole load
+      if (!warp_wait(&bars[BAR_RES_LOADED], (uint32_t)ps & 1, fs, W_RES)) ok = false;
     }
     for (int s = 0; ok && s < A.n_steps; ++s) {
       const int in = (A.cur + s) & 1;

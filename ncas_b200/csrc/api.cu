@@ -691,12 +691,6 @@ int32_t nca_b200_run_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaStat
   if (fire->noise_mode == NCA_NOISE_EXTERNAL && (!fire->noise || n_steps != 1)) return NCA_ERR_INVALID;
   const bool noise = fire->noise_mode != NCA_NOISE_NONE;
   const bool adaptive = fire->mode >= NCA_FIRE_ADAPTIVE_PHILOX;  // fire decisions on the confidence
-  if (adaptive) {
-    // The epilogue part that computes the next step's fire probability must hold the whole
-    // readout slice.
-    const int ch = epi_part_channels(C);
-    if (m->out_offset / ch != (m->out_offset + m->c_out - 1) / ch) return NCA_ERR_UNSUPPORTED;
-  }
   // Fire probabilities of the current state for the first step of each launch (the step kernel
   // keeps them up to date for the following steps).
   auto init_fire_p = [&]() -> int32_t {

@@ -92,7 +92,7 @@ inline int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaSta
     // parts), but no more than spread the batch over every SM.
     if (n_steps < 2 || A.total + 2LL * kTileM >= (1LL << 31)) return NCA_ERR_UNSUPPORTED;
     auto smem_for = [&](long long inst) {
-      return SmemLayout<Cfg>(2, (int)(inst * A.HW), false, A.c_out).total + 1024LL;
+      return SmemLayout<Cfg>(2, (int)(inst * A.HW), false).total + 1024LL;
     };
     long long g_cap = 0;
     while (smem_for(g_cap + 1) <= kMaxSmem && g_cap < A.n_inst) ++g_cap;
@@ -110,10 +110,10 @@ inline int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaSta
     // Window stages: in the hi/lo layout a window lives from the stencil to the epilogue (which
     // reads the hi part of the old state from it), so more stages keep the stencil ahead.
     stages = Cfg::HILO ? kMaxStages : 2;
-    smem = SmemLayout<Cfg>(stages, A.win_cells, A.wimg_lo != nullptr, A.c_out).total + 1024;
+    smem = SmemLayout<Cfg>(stages, A.win_cells, A.wimg_lo != nullptr).total + 1024;
     while (smem > kMaxSmem && stages > 1) {
       --stages;
-      smem = SmemLayout<Cfg>(stages, A.win_cells, A.wimg_lo != nullptr, A.c_out).total + 1024;
+      smem = SmemLayout<Cfg>(stages, A.win_cells, A.wimg_lo != nullptr).total + 1024;
     }
     if (smem > kMaxSmem) return NCA_ERR_UNSUPPORTED;
     grid_ll = A.n_tiles < sms ? A.n_tiles : sms;

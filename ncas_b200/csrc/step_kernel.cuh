@@ -172,14 +172,12 @@ struct StepArgs {
 };
 
 constexpr int kBarSlots = 48;  // mbarriers in the shared-memory layout
-constexpr int kSliceSlots = 1;  // adaptive rules: readout-slice buffers between epilogue and confidence warps
 
 // Shared-memory layout (offsets from a 1024-byte aligned base).
 template <class Cfg>
 struct SmemLayout {
-  int w1, w2, w1lo, w2lo, win, rlo, pwin, slice, b1, b2, flags, bars, misc, total;
-  // c_out: readout channels (the adaptive rules keep each row's readout slice here)
-  __host__ __device__ SmemLayout(int stages, int win_cells, bool lo, int c_out) {
+  int w1, w2, w1lo, w2lo, win, rlo, pwin, b1, b2, flags, bars, misc, total;
+  __host__ __device__ SmemLayout(int stages, int win_cells, bool lo) {
     w1 = 0;
     w2 = w1 + Cfg::W1_BYTES;
     w1lo = w2 + Cfg::W2_BYTES;  // the residual image, when present, follows (same layout)
@@ -189,10 +187,8 @@ struct SmemLayout {
     // resident mode: the window stages are the two buffers of the hi parts of the group's state
     // (win_cells = cells of a group) and the lo parts follow, [chunk][cell][16 B]
     pwin = rlo + (Cfg::RESIDENT ? win_cells * Cfg::ROWB : 0);
-    // adaptive rules: the tile's fire probabilities, one fp32 per row, with each window stage,
-    // and the epilogue's copy of each row's new readout slice (c_out fp32 per row)
-    slice = pwin + (Cfg::ADAPTIVE ? stages * kTileM * 4 : 0);
-    b1 = slice + (Cfg::ADAPTIVE ? kSliceSlots * kTileM * (c_out + 1) * 4 : 0);  // + the row's given flag
+    // adaptive rules: the tile's fire probabilities, one fp32 per row, with each window stage
+    b1 = pwin + (Cfg::ADAPTIVE ? stages * kTileM * 4 : 0);
     b2 = b1 + Cfg::HD * 4;
     flags = b2 + Cfg::C * 4;
     bars = (flags + 4 * kTileM + 7) & ~7;
@@ -256,10 +252,8 @@ enum BarId {
   // +lane quarter + 4 * GEMM1 half (8): the first epilogue part of a half has read its
   // accumulator columns (bf16 mode, two parts per half: the second part writes h over them)
   BAR_PAIR = 30,
-  BAR_SLICE_FULL = 38,   // +slot (2): adaptive rules, the epilogue has written a tile's readout slices
-  BAR_SLICE_EMPTY = 40,  // +slot (2): the confidence warps have read them
-  BAR_RES_LOADED = 42,   // resident mode: the epilogue warps have loaded a group's state
-  BAR_COUNT = 43
+  BAR_RES_LOADED = 38,   // resident mode: the epilogue warps have loaded a group's state
+  BAR_COUNT = 39
 };
 static_assert(BAR_COUNT <= kBarSlots, "barrier area of the shared-memory layout");
 
@@ -476,12 +470,98 @@ __device__ __forceinline__ float adaptive_prob(int mode, float conf, bool given,
   return scale * (1.f - conf) + bias;
 }
 
+// The confidence of a cell (head_readout's conf) for the confidence warps: for the mlp head
+// two scores per packed f32x2 FMA, each accumulated like head_readout's (head_b first, then
+// channels in increasing order, one rounding per fma), so the result is bit-identical.
+__device__ __forceinline__ float head_confidence(int kind, int n_out, int c_out, const float (&hw)[16][16],
+                                                 const float (&hb)[16], const float (&xs)[16]) {
+  if (kind == 1 || c_out > 9) {
+    float conf;
+    int arg;
+    head_readout_auto(kind, n_out, c_out, hw, hb, xs, conf, arg);
+    return conf;
+  }
+  float sc[16];
+#pragma unroll
+  for (int o = 0; o < 16; o += 2) {
+    float2 v = f2(0.f, 0.f);
+    if (o < n_out) {
+      v = f2(hb[o], hb[o + 1]);
+#pragma unroll
+      for (int c = 0; c < 9; ++c) v = __ffma2_rn(f2(hw[o][c], hw[o + 1][c]), f2(xs[c], xs[c]), v);
+    }
+    sc[o] = v.x;
+    sc[o + 1] = v.y;
+  }
+  float best = sc[0];
+#pragma unroll
+  for (int o = 1; o < 16; ++o)
+    if (o < n_out && sc[o] > best) best = sc[o];
+  float den = 0.f;
+#pragma unroll
+  for (int o = 0; o < 16; ++o)
+    if (o < n_out) den += expf(sc[o] - best);
+  return fminf(fmaxf(1.f / den, 0.f), 1.f);
+}
+
+// Row r of tile t of the state the epilogue stored at a step (buffer `out`): its readout slice,
+// channels out_off .. out_off + c_out - 1, to xs[0 .. c_out), zeros after.  The hi/lo layout
+// holds bf16 hi and lo parts in 8-channel chunks (the value is hi + lo), the fp32 layout float4
+// chunks.  The loads are coherent: the epilogue wrote these values during this launch.
+template <class Cfg>
+__device__ __forceinline__ void load_readout_slice(const StepArgs& A, int out, long long t, int r, float (&xs)[16]) {
+  constexpr int CW = Cfg::HILO ? 8 : 4;            // channels per chunk
+  constexpr int NK = Cfg::HILO ? 3 : 5;            // chunks a 16-channel slice can span
+  constexpr int NCHUNK = Cfg::C / CW;
+  const int k0 = A.out_off / CW, d = A.out_off - k0 * CW;
+  const int nk = (d + A.c_out + CW - 1) / CW;
+  float v[NK * CW];
+#pragma unroll
+  for (int j = 0; j < NK; ++j) {
+    const int k = k0 + j;
+    const bool in = j < nk && k < NCHUNK;
+    const long long idx = ((t * NCHUNK + (in ? k : 0)) << 7) + r;
+    if constexpr (Cfg::HILO) {
+      uint4 h = make_uint4(0, 0, 0, 0), l = make_uint4(0, 0, 0, 0);
+      if (in) {
+        h = reinterpret_cast<const uint4*>(A.mirror[out])[idx];
+        l = reinterpret_cast<const uint4*>(A.master[out])[idx];
+      }
+      const uint32_t hh[4] = {h.x, h.y, h.z, h.w}, ll[4] = {l.x, l.y, l.z, l.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        v[j * 8 + 2 * e] = bf16lo_to_f32(hh[e]) + bf16lo_to_f32(ll[e]);
+        v[j * 8 + 2 * e + 1] = bf16hi_to_f32(hh[e]) + bf16hi_to_f32(ll[e]);
+      }
+    } else {
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (in) x = reinterpret_cast<const float4*>(A.master[out])[idx];
+      v[j * 4] = x.x;
+      v[j * 4 + 1] = x.y;
+      v[j * 4 + 2] = x.z;
+      v[j * 4 + 3] = x.w;
+    }
+  }
+  // the slice's offset within its first chunk is uniform: one branch, register moves
+#define NCA_SLICE_AT(D)                                                      \
+  case D:                                                                    \
+    _Pragma("unroll") for (int c = 0; c < 16; ++c) xs[c] = v[(c + D) < NK * CW ? c + D : 0]; \
+    break;
+  switch (d) {
+    NCA_SLICE_AT(0) NCA_SLICE_AT(1) NCA_SLICE_AT(2) NCA_SLICE_AT(3)
+    NCA_SLICE_AT(4) NCA_SLICE_AT(5) NCA_SLICE_AT(6) NCA_SLICE_AT(7)
+  }
+#undef NCA_SLICE_AT
+#pragma unroll
+  for (int c = 0; c < 16; ++c) xs[c] = c < A.c_out ? xs[c] : 0.f;
+}
+
 template <class Cfg>
 __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_constant__ StepArgs A) {
   using namespace nca;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  const SmemLayout<Cfg> L(A.stages, A.win_cells, A.wimg_lo != nullptr, A.c_out);
+  const SmemLayout<Cfg> L(A.stages, A.win_cells, A.wimg_lo != nullptr);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L.misc);
   int* abort_flag = reinterpret_cast<int*>(smem + L.misc + 8);
@@ -528,10 +608,6 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
     for (int r = 0; r < 8; ++r) mbar_init(&bars[BAR_PAIR + r], 1);
     mbar_init(&bars[BAR_RES_LOADED], Cfg::EPI_WARPS);
     for (int i = 0; i < 8; ++i) reinterpret_cast<unsigned*>(smem + L.misc + 32)[i] = 0u;
-    for (int r = 0; r < kSliceSlots; ++r) {
-      mbar_init(&bars[BAR_SLICE_FULL + r], 4);   // the 4 epilogue warps of the part holding the slice
-      mbar_init(&bars[BAR_SLICE_EMPTY + r], 2);  // the 2 confidence warps
-    }
     fence_mbar_init();
   }
   // Every chunk row of a window stage ends with a padding cell (index win_cells): the stencil
@@ -854,36 +930,34 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
     __syncwarp();
   } else if (Cfg::ADAPTIVE) {
     // ---------------------------------------------------------------- confidence (warps 2, 3)
-    // Adaptive rules: per tile, the readout slices of the new state (copied to shared memory by
-    // the epilogue) -> head_readout -> the cell's fire probability of the next step, 2 rows per
-    // lane.  The stores count for the step end like the epilogue's.
+    // Adaptive rules: per tile, once every epilogue warp has stored the tile's new state (their
+    // progress words), the readout slice of each row is read back from global memory (L2) ->
+    // the head -> the cell's fire probability of the next step, 2 rows per lane.  The epilogue
+    // never waits for these warps within a step; their stores count for the step end like the
+    // epilogue's.
     const int cw = warp - 2;
+    const unsigned* s_prog = reinterpret_cast<const unsigned*>(smem + L.misc + 32);
     uint32_t it = 0;
     bool ok = true;
     for (int s = 0; ok && s < A.n_steps; ++s) {
+      const int out = (A.cur + s + 1) & 1;
       for (long long t = blockIdx.x; t < A.n_tiles; t += grid, ++it) {
-        const int sl = (int)(it % kSliceSlots);
-        const uint32_t sph = (it / kSliceSlots) & 1;
-        const float* slice = reinterpret_cast<const float*>(smem + L.slice) + sl * kTileM * (A.c_out + 1);
-        if (!warp_wait(&bars[BAR_SLICE_FULL + sl], sph, fs, W_CONF)) { ok = false; break; }
+        if (!wait_progress(s_prog, Cfg::EPI_WARPS, it + 1u, fs, W_CONF)) { ok = false; break; }
+        float xs[2][16];
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) load_readout_slice<Cfg>(A, out, t, cw * 64 + rr * 32 + lane, xs[rr]);
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr) {
-          const int r = cw * 64 + rr * 32 + lane;
-          const long long g = t * kTileM + r;
-          if (g < total) {
-            const float* row = slice + r * (A.c_out + 1);
-            float xs[16];
-#pragma unroll
-            for (int c = 0; c < 16; ++c) xs[c] = c < A.c_out ? row[c] : 0.f;
-            float conf;
-            int arg;
-            head_readout_auto(A.head_kind, A.n_out, A.c_out, A.head_w, A.head_b, xs, conf, arg);
-            A.fire_p[g] = adaptive_prob(A.fire_mode, conf, row[A.c_out] != 0.f, A.ad_scale, A.ad_bias,
-                                        A.p_low, A.tau, A.p_fire, A.given_confident);
+          const unsigned g = (unsigned)(t * kTileM) + (unsigned)(cw * 64 + rr * 32 + lane);
+          if ((long long)g < total) {
+            const int inst = (int)fdiv(g, A.div_hw);
+            const int p = (int)(g - (unsigned)inst * A.HW);
+            const int row = A.inst_row ? A.inst_row[inst] : (int)fdiv((unsigned)inst, A.div_k);
+            const float conf = head_confidence(A.head_kind, A.n_out, A.c_out, A.head_w, A.head_b, xs[rr]);
+            A.fire_p[g] = adaptive_prob(A.fire_mode, conf, A.given[(long long)row * A.HW + p] != 0, A.ad_scale,
+                                        A.ad_bias, A.p_low, A.tau, A.p_fire, A.given_confident);
           }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive_relaxed(&bars[BAR_SLICE_EMPTY + sl]);
         if constexpr (Cfg::TILEDEP) {
           __syncwarp();
           if (lane == 0) asm volatile("red.release.cta.shared::cta.add.u32 [%0], 1;" ::"r"(smem_u32(s_tiles_done)) : "memory");
@@ -1333,13 +1407,6 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_relaxed(&bars[BAR_ACC_EMPTY + rg]);
-        // Adaptive rules: the part that holds the readout slice writes it to shared memory once the
-        // confidence warps have read the previous tile's.
-        const bool slice_here = Cfg::ADAPTIVE && part == A.out_off / CH;
-        if constexpr (Cfg::ADAPTIVE) {
-          if (slice_here && !warp_wait(&bars[BAR_SLICE_EMPTY + (int)(it % kSliceSlots)],
-                                       ((it / kSliceSlots) & 1) ^ 1, fs, W_CONF)) { ok = false; break; }
-        }
         if (valid) {
           const float4* bb = reinterpret_cast<const float4*>(s_b2 + part * CH);
           const float2 ff = f2(f, f);
@@ -1364,14 +1431,6 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
           bool nz = false;
           int p_cell = 0;
           long long nid = 0;
-          // Adaptive rules: the part that holds the readout slice copies the values it stores for
-          // those channels (and the given flag) to the row's slice in shared memory; the
-          // confidence warps compute the cell's fire probability of the next step from them.
-          float* s_slice = reinterpret_cast<float*>(smem + L.slice) +
-                           ((int)(it % kSliceSlots) * kTileM + m) * (A.c_out + 1);
-          if constexpr (Cfg::ADAPTIVE) {
-            if (slice_here) s_slice[A.c_out] = gv ? 1.f : 0.f;
-          }
           if constexpr (Cfg::NOISE) {
             p_cell = (int)(g - (unsigned)inst * A.HW);
             nid = A.inst_offset + (A.inst_id ? A.inst_id[inst] : inst);
@@ -1447,12 +1506,6 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
               pk[2 * (q & 1) + 1] = h1;
               pl[2 * (q & 1)] = pack_bf16(y0.x - bf16lo_to_f32(h0), y0.y - bf16hi_to_f32(h0));
               pl[2 * (q & 1) + 1] = pack_bf16(y1.x - bf16lo_to_f32(h1), y1.y - bf16hi_to_f32(h1));
-              if (Cfg::ADAPTIVE && slice_here) {
-                // the stored state hi + lo of these 4 channels
-                const uint32_t l0 = pl[2 * (q & 1)], l1 = pl[2 * (q & 1) + 1];
-                y0 = f2(bf16lo_to_f32(h0) + bf16lo_to_f32(l0), bf16hi_to_f32(h0) + bf16hi_to_f32(l0));
-                y1 = f2(bf16lo_to_f32(h1) + bf16lo_to_f32(l1), bf16hi_to_f32(h1) + bf16hi_to_f32(l1));
-              }
               if (q & 1) {
                 mout4[(q >> 1) << 7] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 lout4[(q >> 1) << 7] = make_uint4(pl[0], pl[1], pl[2], pl[3]);
@@ -1465,21 +1518,6 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
                 if (q & 1) mout4[(q >> 1) << 7] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
               }
             }
-            if constexpr (Cfg::ADAPTIVE) {
-              if (slice_here) {
-                const int cb = part * CH + 4 * q - A.out_off;  // slice index of the chunk's channel 0
-                const float vv[4] = {y0.x, y0.y, y1.x, y1.y};
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                  if (cb + e >= 0 && cb + e < A.c_out) s_slice[cb + e] = vv[e];
-              }
-            }
-          }
-        }
-        if constexpr (Cfg::ADAPTIVE) {
-          if (slice_here) {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars[BAR_SLICE_FULL + (int)(it % kSliceSlots)]);
           }
         }
         if (part == 0 && A.updates != nullptr) {
@@ -1491,9 +1529,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
             if (cnt) atomicAdd(&A.updates[inst], (unsigned)cnt);
           }
         }
-        if constexpr (Cfg::RESIDENT) {
-          // this warp is done with the tile (its shared-memory stores are ordered before the
-          // release): the stencil's wait for the next step reads it
+        if constexpr (Cfg::RESIDENT || Cfg::ADAPTIVE) {
+          // this warp is done with the tile (its stores are ordered before the release): the
+          // resident stencil's wait for the next step, or the confidence warps, read it
           __syncwarp();
           if (lane == 0)
             asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(s_prog + ew)), "r"(it + 1u) : "memory");

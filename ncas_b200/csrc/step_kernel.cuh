@@ -172,11 +172,16 @@ struct StepArgs {
 };
 
 constexpr int kBarSlots = 48;  // mbarriers in the shared-memory layout
+constexpr int kHeadFloats = 16 * 16 + 16;  // a copy of the readout head in shared memory
+template <int N>
+struct IntTag {
+  static constexpr int value = N;
+};
 
 // Shared-memory layout (offsets from a 1024-byte aligned base).
 template <class Cfg>
 struct SmemLayout {
-  int w1, w2, w1lo, w2lo, win, rlo, pwin, b1, b2, flags, bars, misc, total;
+  int w1, w2, w1lo, w2lo, win, rlo, pwin, head, b1, b2, flags, bars, misc, total;
   __host__ __device__ SmemLayout(int stages, int win_cells, bool lo) {
     w1 = 0;
     w2 = w1 + Cfg::W1_BYTES;
@@ -187,8 +192,10 @@ struct SmemLayout {
     // resident mode: the window stages are the two buffers of the hi parts of the group's state
     // (win_cells = cells of a group) and the lo parts follow, [chunk][cell][16 B]
     pwin = rlo + (Cfg::RESIDENT ? win_cells * Cfg::ROWB : 0);
-    // adaptive rules: the tile's fire probabilities, one fp32 per row, with each window stage
-    b1 = pwin + (Cfg::ADAPTIVE ? stages * kTileM * 4 : 0);
+    // adaptive rules: the tile's fire probabilities, one fp32 per row, with each window stage,
+    // and each confidence warp's copy of the head (16 x 16 weights, 16 biases)
+    head = pwin + (Cfg::ADAPTIVE ? stages * kTileM * 4 : 0);
+    b1 = head + (Cfg::ADAPTIVE ? 2 * kHeadFloats * 4 : 0);
     b2 = b1 + Cfg::HD * 4;
     flags = b2 + Cfg::C * 4;
     bars = (flags + 4 * kTileM + 7) & ~7;
@@ -470,82 +477,110 @@ __device__ __forceinline__ float adaptive_prob(int mode, float conf, bool given,
   return scale * (1.f - conf) + bias;
 }
 
-// The confidence of a cell (head_readout's conf) for the confidence warps: for the mlp head
-// two scores per packed f32x2 FMA, each accumulated like head_readout's (head_b first, then
-// channels in increasing order, one rounding per fma), so the result is bit-identical.
-__device__ __forceinline__ float head_confidence(int kind, int n_out, int c_out, const float (&hw)[16][16],
-                                                 const float (&hb)[16], const float (&xs)[16]) {
-  if (kind == 1 || c_out > 9) {
-    float conf;
-    int arg;
-    head_readout_auto(kind, n_out, c_out, hw, hb, xs, conf, arg);
-    return conf;
-  }
-  float sc[16];
+// The confidences of NR cells (head_readout's conf) for the confidence warps, mlp head: the
+// weights come from this warp's copy in shared memory (hw [16][16], then hb [16]; broadcast
+// loads shared by the cells) and two scores per packed f32x2 FMA, each accumulated like
+// head_readout's (head_b first, then channels in increasing order, one rounding per fma), so
+// the results are bit-identical to it.  MAXC / MAXO bound c_out / n_out at compile time: the
+// code has no branch (scores past n_out are masked out of the max and the sum), so the
+// compiler interleaves the independent FMA chains.
+template <int MAXC, int MAXO, int NR>
+__device__ __forceinline__ void head_confidence(int n_out, const float* s_head, const float (&x)[NR][MAXC],
+                                                float (&conf)[NR]) {
+  static_assert(MAXO % 2 == 0 && MAXO <= 16 && MAXC <= 16, "head bounds");
+  float sc[NR][MAXO];
 #pragma unroll
-  for (int o = 0; o < 16; o += 2) {
-    float2 v = f2(0.f, 0.f);
-    if (o < n_out) {
-      v = f2(hb[o], hb[o + 1]);
+  for (int o = 0; o < MAXO; o += 2) {
+    float2 v[NR];
+    const float2 bias = *reinterpret_cast<const float2*>(s_head + 256 + o);
 #pragma unroll
-      for (int c = 0; c < 9; ++c) v = __ffma2_rn(f2(hw[o][c], hw[o + 1][c]), f2(xs[c], xs[c]), v);
+    for (int q = 0; q < NR; ++q) v[q] = bias;
+#pragma unroll
+    for (int c = 0; c < MAXC; ++c) {
+      const float2 w = f2(s_head[o * 16 + c], s_head[(o + 1) * 16 + c]);
+#pragma unroll
+      for (int q = 0; q < NR; ++q) v[q] = __ffma2_rn(w, f2(x[q][c], x[q][c]), v[q]);
     }
-    sc[o] = v.x;
-    sc[o + 1] = v.y;
+#pragma unroll
+    for (int q = 0; q < NR; ++q) {
+      sc[q][o] = v[q].x;
+      sc[q][o + 1] = v[q].y;
+    }
   }
-  float best = sc[0];
 #pragma unroll
-  for (int o = 1; o < 16; ++o)
-    if (o < n_out && sc[o] > best) best = sc[o];
-  float den = 0.f;
+  for (int q = 0; q < NR; ++q) {
+    float b = sc[q][0];
 #pragma unroll
-  for (int o = 0; o < 16; ++o)
-    if (o < n_out) den += expf(sc[o] - best);
-  return fminf(fmaxf(1.f / den, 0.f), 1.f);
+    for (int o = 1; o < MAXO; ++o) b = (o < n_out && sc[q][o] > b) ? sc[q][o] : b;
+    float d = 0.f;
+#pragma unroll
+    for (int o = 0; o < MAXO; ++o) {
+      const float e = expf(sc[q][o] - b);
+      d += o < n_out ? e : 0.f;
+    }
+    conf[q] = fminf(fmaxf(1.f / d, 0.f), 1.f);
+  }
 }
 
 // Row r of tile t of the state the epilogue stored at a step (buffer `out`): its readout slice,
-// channels out_off .. out_off + c_out - 1, to xs[0 .. c_out), zeros after.  The hi/lo layout
-// holds bf16 hi and lo parts in 8-channel chunks (the value is hi + lo), the fp32 layout float4
-// chunks.  The loads are coherent: the epilogue wrote these values during this launch.
-template <class Cfg>
-__device__ __forceinline__ void load_readout_slice(const StepArgs& A, int out, long long t, int r, float (&xs)[16]) {
-  constexpr int CW = Cfg::HILO ? 8 : 4;            // channels per chunk
-  constexpr int NK = Cfg::HILO ? 3 : 5;            // chunks a 16-channel slice can span
-  constexpr int NCHUNK = Cfg::C / CW;
-  const int k0 = A.out_off / CW, d = A.out_off - k0 * CW;
-  const int nk = (d + A.c_out + CW - 1) / CW;
-  float v[NK * CW];
+// channels out_off .. out_off + c_out - 1 (c_out <= MAXC).  slice_issue loads the chunks that
+// hold it (the hi/lo layout: bf16 hi and lo parts in 8-channel chunks, the value is hi + lo; the
+// fp32 layout: float4 chunks) without using them, so their latency overlaps other work;
+// slice_values converts them to xs[0 .. c_out), zeros after.  The loads are coherent: the
+// epilogue wrote these values during this launch.
+template <class Cfg, int MAXC>
+struct SliceRaw {
+  static constexpr int CW = Cfg::HILO ? 8 : 4;              // channels per chunk
+  static constexpr int NK = (2 * (CW - 1) + MAXC) / CW;      // chunks a slice can span
+  uint4 w[Cfg::HILO ? 2 * NK : NK];                          // hi chunks then lo chunks / float4 bits
+};
+
+template <class Cfg, int MAXC>
+__device__ __forceinline__ void slice_issue(const StepArgs& A, int out, long long t, int r, SliceRaw<Cfg, MAXC>& R) {
+  using S = SliceRaw<Cfg, MAXC>;
+  constexpr int NCHUNK = Cfg::C / S::CW;
+  const int k0 = A.out_off / S::CW, d = A.out_off - k0 * S::CW;
+  const int nk = (d + A.c_out + S::CW - 1) / S::CW;
 #pragma unroll
-  for (int j = 0; j < NK; ++j) {
+  for (int j = 0; j < S::NK; ++j) {
     const int k = k0 + j;
     const bool in = j < nk && k < NCHUNK;
     const long long idx = ((t * NCHUNK + (in ? k : 0)) << 7) + r;
     if constexpr (Cfg::HILO) {
-      uint4 h = make_uint4(0, 0, 0, 0), l = make_uint4(0, 0, 0, 0);
-      if (in) {
-        h = reinterpret_cast<const uint4*>(A.mirror[out])[idx];
-        l = reinterpret_cast<const uint4*>(A.master[out])[idx];
-      }
-      const uint32_t hh[4] = {h.x, h.y, h.z, h.w}, ll[4] = {l.x, l.y, l.z, l.w};
+      R.w[j] = in ? reinterpret_cast<const uint4*>(A.mirror[out])[idx] : make_uint4(0, 0, 0, 0);
+      R.w[S::NK + j] = in ? reinterpret_cast<const uint4*>(A.master[out])[idx] : make_uint4(0, 0, 0, 0);
+    } else {
+      R.w[j] = in ? reinterpret_cast<const uint4*>(A.master[out])[idx] : make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+template <class Cfg, int MAXC>
+__device__ __forceinline__ void slice_values(const StepArgs& A, const SliceRaw<Cfg, MAXC>& R, float (&xs)[MAXC]) {
+  using S = SliceRaw<Cfg, MAXC>;
+  const int d = A.out_off % S::CW;
+  float v[S::NK * S::CW];
+#pragma unroll
+  for (int j = 0; j < S::NK; ++j) {
+    if constexpr (Cfg::HILO) {
+      const uint32_t hh[4] = {R.w[j].x, R.w[j].y, R.w[j].z, R.w[j].w};
+      const uint32_t ll[4] = {R.w[S::NK + j].x, R.w[S::NK + j].y, R.w[S::NK + j].z, R.w[S::NK + j].w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         v[j * 8 + 2 * e] = bf16lo_to_f32(hh[e]) + bf16lo_to_f32(ll[e]);
         v[j * 8 + 2 * e + 1] = bf16hi_to_f32(hh[e]) + bf16hi_to_f32(ll[e]);
       }
     } else {
-      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (in) x = reinterpret_cast<const float4*>(A.master[out])[idx];
-      v[j * 4] = x.x;
-      v[j * 4 + 1] = x.y;
-      v[j * 4 + 2] = x.z;
-      v[j * 4 + 3] = x.w;
+      v[j * 4] = __uint_as_float(R.w[j].x);
+      v[j * 4 + 1] = __uint_as_float(R.w[j].y);
+      v[j * 4 + 2] = __uint_as_float(R.w[j].z);
+      v[j * 4 + 3] = __uint_as_float(R.w[j].w);
     }
   }
   // the slice's offset within its first chunk is uniform: one branch, register moves
-#define NCA_SLICE_AT(D)                                                      \
-  case D:                                                                    \
-    _Pragma("unroll") for (int c = 0; c < 16; ++c) xs[c] = v[(c + D) < NK * CW ? c + D : 0]; \
+#define NCA_SLICE_AT(D)                                                                        \
+  case D:                                                                                      \
+    _Pragma("unroll") for (int c = 0; c < MAXC; ++c) xs[c] = v[(c + D) < S::NK * S::CW ? c + D : 0]; \
     break;
   switch (d) {
     NCA_SLICE_AT(0) NCA_SLICE_AT(1) NCA_SLICE_AT(2) NCA_SLICE_AT(3)
@@ -553,7 +588,7 @@ __device__ __forceinline__ void load_readout_slice(const StepArgs& A, int out, l
   }
 #undef NCA_SLICE_AT
 #pragma unroll
-  for (int c = 0; c < 16; ++c) xs[c] = c < A.c_out ? xs[c] : 0.f;
+  for (int c = 0; c < MAXC; ++c) xs[c] = c < A.c_out ? xs[c] : 0.f;
 }
 
 template <class Cfg>
@@ -937,47 +972,97 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
     // epilogue's.
     const int cw = warp - 2;
     const unsigned* s_prog = reinterpret_cast<const unsigned*>(smem + L.misc + 32);
+    float* s_head = reinterpret_cast<float*>(smem + L.head) + cw * kHeadFloats;
+    for (int i = lane; i < kHeadFloats; i += 32) s_head[i] = i < 256 ? A.head_w[i >> 4][i & 15] : A.head_b[i - 256];
+    __syncwarp();
+    // Each warp evaluates rows cw * 64 + lane and cw * 64 + 32 + lane of every tile: the loads of
+    // both rows are issued before either is used.  Fast path (mlp head, c_out <= 9, n_out <= 10):
+    // 9 channels per row, the head row by row; the general head keeps 16 channels per row.
     uint32_t it = 0;
     bool ok = true;
-    for (int s = 0; ok && s < A.n_steps; ++s) {
-      const int out = (A.cur + s + 1) & 1;
-      for (long long t = blockIdx.x; t < A.n_tiles; t += grid, ++it) {
-        if (!wait_progress(s_prog, Cfg::EPI_WARPS, it + 1u, fs, W_CONF)) { ok = false; break; }
-        float xs[2][16];
-#pragma unroll
-        for (int rr = 0; rr < 2; ++rr) load_readout_slice<Cfg>(A, out, t, cw * 64 + rr * 32 + lane, xs[rr]);
-#pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-          const unsigned g = (unsigned)(t * kTileM) + (unsigned)(cw * 64 + rr * 32 + lane);
-          if ((long long)g < total) {
-            const int inst = (int)fdiv(g, A.div_hw);
-            const int p = (int)(g - (unsigned)inst * A.HW);
-            const int row = A.inst_row ? A.inst_row[inst] : (int)fdiv((unsigned)inst, A.div_k);
-            const float conf = head_confidence(A.head_kind, A.n_out, A.c_out, A.head_w, A.head_b, xs[rr]);
-            A.fire_p[g] = adaptive_prob(A.fire_mode, conf, A.given[(long long)row * A.HW + p] != 0, A.ad_scale,
-                                        A.ad_bias, A.p_low, A.tau, A.p_fire, A.given_confident);
-          }
+    auto conf_loop = [&](auto maxc_tag) {
+      constexpr int MAXC = decltype(maxc_tag)::value;
+      struct Row {
+        SliceRaw<Cfg, MAXC> raw;
+        unsigned g;  // global cell
+        int given;   // the cell's given byte
+      };
+      auto issue = [&](Row& R, long long t, int out, int rr) {
+        const int r = cw * 64 + rr * 32 + lane;
+        slice_issue<Cfg, MAXC>(A, out, t, r, R.raw);
+        R.g = (unsigned)(t * kTileM) + (unsigned)r;
+        R.given = 0;
+        if ((long long)R.g < total) {
+          const int inst = (int)fdiv(R.g, A.div_hw);
+          const int p = (int)(R.g - (unsigned)inst * A.HW);
+          const int row = A.inst_row ? A.inst_row[inst] : (int)fdiv((unsigned)inst, A.div_k);
+          R.given = A.given[(long long)row * A.HW + p];
         }
+      };
+      auto store = [&](const Row& R, float conf) {
+        if ((long long)R.g < total)
+          A.fire_p[R.g] = adaptive_prob(A.fire_mode, conf, R.given != 0, A.ad_scale, A.ad_bias, A.p_low,
+                                        A.tau, A.p_fire, A.given_confident);
+      };
+      auto tile_done = [&]() {
         if constexpr (Cfg::TILEDEP) {
           __syncwarp();
           if (lane == 0) asm volatile("red.release.cta.shared::cta.add.u32 [%0], 1;" ::"r"(smem_u32(s_tiles_done)) : "memory");
         }
+      };
+      auto finish1 = [&](const Row& R) {
+        float x[1][MAXC], conf[1];
+        slice_values<Cfg, MAXC>(A, R.raw, x[0]);
+        head_confidence<MAXC, 10, 1>(A.n_out, s_head, x, conf);
+        store(R, conf[0]);
+      };
+      Row ra, rb;
+      for (int s = 0; ok && s < A.n_steps; ++s) {
+        const int out = (A.cur + s + 1) & 1;
+        for (long long t = blockIdx.x; t < A.n_tiles; t += grid, ++it) {
+          if (!wait_progress(s_prog, Cfg::EPI_WARPS, it + 1u, fs, W_CONF)) { ok = false; break; }
+          issue(ra, t, out, 0);
+          issue(rb, t, out, 1);
+          if constexpr (MAXC == 9) {
+            finish1(ra);
+            finish1(rb);
+            tile_done();
+          } else {
+            float x[2][MAXC], conf[2];
+            slice_values<Cfg, MAXC>(A, ra.raw, x[0]);
+            slice_values<Cfg, MAXC>(A, rb.raw, x[1]);
+            if (A.head_kind != 0) {
+#pragma unroll
+              for (int rr = 0; rr < 2; ++rr) {
+                int arg;
+                head_readout_auto(A.head_kind, A.n_out, A.c_out, A.head_w, A.head_b, x[rr], conf[rr], arg);
+              }
+            } else {
+              head_confidence<16, 16, 2>(A.n_out, s_head, x, conf);
+            }
+            store(ra, conf[0]);
+            store(rb, conf[1]);
+            tile_done();
+          }
+        }
+        if constexpr (!Cfg::TILEDEP) {
+          // the step end of the epilogue warps, joined by these two warps (their stores of the step
+          // are then covered by the epilogue's fence before the step counter)
+          unsigned any_fail;
+          asm volatile(
+              "{\n\t.reg .pred p, q;\n\t"
+              "setp.ne.u32 p, %1, 0;\n\t"
+              "bar.red.or.pred q, 1, %2, p;\n\t"
+              "selp.u32 %0, 1, 0, q;\n\t}"
+              : "=r"(any_fail)
+              : "r"((unsigned)(!ok || *(volatile int*)abort_flag != 0)), "n"(Cfg::EPI_WARPS * 32 + 64)
+              : "memory");
+          if (any_fail) { ok = false; break; }
+        }
       }
-      if constexpr (!Cfg::TILEDEP) {
-        // the step end of the epilogue warps, joined by these two warps (their stores of the step
-        // are then covered by the epilogue's fence before the step counter)
-        unsigned any_fail;
-        asm volatile(
-            "{\n\t.reg .pred p, q;\n\t"
-            "setp.ne.u32 p, %1, 0;\n\t"
-            "bar.red.or.pred q, 1, %2, p;\n\t"
-            "selp.u32 %0, 1, 0, q;\n\t}"
-            : "=r"(any_fail)
-            : "r"((unsigned)(!ok || *(volatile int*)abort_flag != 0)), "n"(Cfg::EPI_WARPS * 32 + 64)
-            : "memory");
-        if (any_fail) { ok = false; break; }
-      }
-    }
+    };
+    if (A.head_kind == 0 && A.c_out <= 9 && A.n_out <= 10) conf_loop(IntTag<9>{});
+    else conf_loop(IntTag<16>{});
   }  // without the adaptive rules, warps 2 and 3 are idle
   } else if (!skip && warp >= kStencilWarp0 && warp < kEpiWarp0) {
     // ---------------------------------------------------------------- stencil

@@ -181,16 +181,22 @@ def run_reference(args) -> None:
 
 
 # --------------------------------------------------------------------------------- GPU arm
-def roofline(bc, precision: str, kdur_ms: list[float], cells: list[int]) -> dict:
+def roofline(bc, precision: str, kdur_ms: list[float], cells: list[int], steps: list[int],
+             resident: bool) -> dict:
     """The step kernel's roofline from its CUDA-event launch times: the lower of the tensor
-    ceiling (GEMM FLOPs) and the HBM ceiling (algorithmic bytes) per cell-update."""
+    ceiling (GEMM FLOPs) and the HBM ceiling (algorithmic bytes) per cell-update.  cells: the
+    cell-updates of each launch, steps: its steps; resident: the launches with more than one
+    step ran the shared-memory-resident kernel, which reads the fp32 state once (4C bytes per
+    cell) and writes it and its bf16 copy once (6C) per launch."""
     pk, pk_kind = peaks()
     flop_per_cu = bc.flop_per_cell_update
     # split mode runs every GEMM on the hi and the lo part of its activations: twice the MMAs
     executed = flop_per_cu * (2 if precision == "split" else 1)
     avg_kms = float(np.mean(kdur_ms))
     avg_cells = float(np.mean(cells))
-    bytes_per_cu = bc.bytes_per_cell_update(precision)
+    stream_b = bc.bytes_per_cell_update(precision)
+    per_launch = [c * (10 * bc.channels / n if resident and n > 1 else stream_b) for c, n in zip(cells, steps)]
+    bytes_per_cu = float(sum(per_launch)) / float(sum(cells))
     tb = profile_traffic(bc.name) if precision == "bf16" else None
     t_peak = pk.get("bf16_tflops_sustained", 1400.0)
     t_burst = pk.get("bf16_tflops", 1590.0)
@@ -210,7 +216,7 @@ def roofline(bc, precision: str, kdur_ms: list[float], cells: list[int]) -> dict
         roof["executed_tflops"] = executed * avg_cells / (avg_kms / 1e3) / 1e12
     roof.update({"traffic": None if tb is None else tb * avg_cells, "kernel": "nca_step_kernel",
                  "flop_per_cell_update": flop_per_cu, "bytes_per_cell_update": bytes_per_cu,
-                 "kernel_ms": avg_kms})
+                 "kernel_ms": avg_kms, "resident": resident})
     return roof
 
 
@@ -277,7 +283,7 @@ def run_ours(args) -> None:
         batch = eng.batch_from_boards(shard.inputs, shard.given, K, inst_offset=s * K)
         st = eng.new_state(n * K, HW)
         updates = torch.zeros(n * K, dtype=torch.int32, device=dev)
-        kern, kern_cells = [], []
+        kern, kern_cells, kern_steps = [], [], []
 
         def one_step(timed: bool):
             eng.init_state(st, batch)
@@ -292,6 +298,7 @@ def run_ours(args) -> None:
                 if timed:
                     kern.append((ev0, ev1))
                     kern_cells.append(n * K * HW * (b - a))
+                    kern_steps.append(b - a)
                 if b < bc.depth:
                     r = eng.readout(st, batch)
                     eng.prune_refill(st, r["pred"], r["board_conf"], n, K, bc.n_cap)
@@ -317,7 +324,9 @@ def run_ours(args) -> None:
         eng.check()
         ms = max_over_ranks(t0.elapsed_time(t1))
         kdur = [a.elapsed_time(b) for a, b in kern]
-        return ms, kdur, kern_cells, eng.launches - l0, clk.summary(), st.buffer.numel(), model
+        res = (precision == "bf16" and not adaptive and not args.no_resident
+               and eng.resident_group(shard.inputs.shape[1], shard.inputs.shape[2]) >= 1)
+        return ms, kdur, (kern_cells, kern_steps, res), eng.launches - l0, clk.summary(), st.buffer.numel(), model
 
     ms, kdur, kcells, launches, clocks, state_bytes, model = measure(args.precision, args.steps,
                                                                      args.warmup, True)
@@ -353,7 +362,7 @@ def run_ours(args) -> None:
         sms, skdur, skcells, _, _, _, _ = measure("split", max(1, min(args.steps, 3)), 1, False)
         split = {"value": total_cu * max(1, min(args.steps, 3)) / (sms / 1e3),
                  "ms_per_step": sms / max(1, min(args.steps, 3)),
-                 "roofline": roofline(bc, "split", skdur, skcells)}
+                 "roofline": roofline(bc, "split", skdur, *skcells)}
 
     if rank == 0:
         line = {
@@ -366,7 +375,7 @@ def run_ours(args) -> None:
                        "resident": not args.no_resident,
                        "parallelism": f"{n_total} boards over {world} GPU(s), all K trials of a board on one GPU",
                        "l2": f"state {state_bytes / 1e9:.2f} GB per GPU vs 126 MB L2"},
-            "roofline": roofline(bc, args.precision, kdur, kcells),
+            "roofline": roofline(bc, args.precision, kdur, *kcells),
             "e2e": None if e2e_value is None else {
                 "value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,

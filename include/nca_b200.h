@@ -201,6 +201,14 @@ int32_t nca_b200_state_store_nchw(const NcaState* st, float* x_nchw, void* strea
 int32_t nca_b200_run_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaState* st,
                            int32_t n_steps, const NcaFireDesc* fire, int32_t* ctrl,
                            int32_t timeout_ms, void* stream);
+/* The shared-memory-resident form of the step (NcaFireDesc.resident): the number of whole
+ * instances of a height x width board that one CTA keeps in shared memory for all steps of a
+ * launch, 0 when the model's shape has no resident kernel (64 channels) or not even one instance
+ * fits.  A launch with resident = 1 runs the resident kernel exactly when this is at least 1, the
+ * state precision is bf16, the fire rule is not a confidence rule, there is no state noise and
+ * n_steps > 1; the state is then read once and written once per launch.  An addition of this
+ * library (the reference steps every batch through global memory). */
+int32_t nca_b200_resident_group(const NcaModelDesc* m, int32_t height, int32_t width);
 
 /* ---- readout, selection, pruning ---------------------------------------------------------- */
 /* Per cell: argmax token of the mlp head (given cells show their input token) and max-softmax

@@ -131,6 +131,7 @@ SIGNATURES = {
     ),
     "nca_b200_state_load_nchw": (_I, [C.POINTER(NcaState), _P, _P]),
     "nca_b200_state_store_nchw": (_I, [C.POINTER(NcaState), _P, _P]),
+    "nca_b200_resident_group": (_I, [C.POINTER(NcaModelDesc), _I, _I]),
     "nca_b200_run_steps": (
         _I,
         [

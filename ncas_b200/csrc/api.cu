@@ -860,6 +860,15 @@ int32_t nca_b200_gather(const NcaState* src, NcaState* dst, const int32_t* sel, 
   return cuda_status(cudaGetLastError());
 }
 
+int32_t nca_b200_resident_group(const NcaModelDesc* m, int32_t height, int32_t width) {
+  if (!m || height < 1 || width < 1) return 0;
+  const long long hw = (long long)height * width;
+  if (m->channels == 32 && m->hidden == 128) return resident_capacity_32_128(hw);
+  if (m->channels == 16 && m->hidden == 128) return resident_capacity_16_128(hw);
+  if (m->channels == 32 && m->hidden == 256) return resident_capacity_32_256(hw);
+  return 0;
+}
+
 int32_t nca_b200_ctrl_status(int32_t* ctrl, int32_t* detail, void* stream) {
   if (!ctrl) return NCA_ERR_INVALID;
   cudaStream_t s = as_stream(stream);

@@ -15,6 +15,18 @@ namespace nca {
 
 constexpr int kMaxSmem = 232448;  // opt-in dynamic shared memory per CTA on sm_100
 
+// Resident kernel: the most whole instances of `hw` cells one CTA keeps in shared memory (the
+// two buffers of hi parts, the lo parts and the weights), 0 when not even one fits.
+template <class Cfg>
+inline int32_t resident_capacity(long long hw) {
+  static_assert(Cfg::RESIDENT, "resident kernel shapes only");
+  if (hw < 1 || hw > kMaxSmem) return 0;
+  auto smem_for = [&](long long inst) { return SmemLayout<Cfg>(2, (int)(inst * hw), false).total + 1024LL; };
+  int32_t g = 0;
+  while (smem_for(g + 1) <= kMaxSmem) ++g;
+  return g;
+}
+
 template <class Cfg>
 inline int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaState* st, int32_t n_steps,
                      const NcaFireDesc* fire, int32_t* ctrl, int32_t timeout_ms,
@@ -91,11 +103,8 @@ inline int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaSta
     // Groups of whole instances: as many as fit the shared memory (the two hi buffers and the lo
     // parts), but no more than spread the batch over every SM.
     if (n_steps < 2 || A.total + 2LL * kTileM >= (1LL << 31)) return NCA_ERR_UNSUPPORTED;
-    auto smem_for = [&](long long inst) {
-      return SmemLayout<Cfg>(2, (int)(inst * A.HW), false).total + 1024LL;
-    };
-    long long g_cap = 0;
-    while (smem_for(g_cap + 1) <= kMaxSmem && g_cap < A.n_inst) ++g_cap;
+    long long g_cap = resident_capacity<Cfg>(A.HW);
+    if (g_cap > A.n_inst) g_cap = A.n_inst;
     if (g_cap < 1) return NCA_ERR_UNSUPPORTED;
     const long long spread = (A.n_inst + sms - 1) / sms;
     const long long g = g_cap < spread ? g_cap : spread;
@@ -104,7 +113,7 @@ inline int32_t launch_steps(const NcaModelDesc* m, const NcaBatchDesc* b, NcaSta
     A.n_groups = (A.n_inst + g - 1) / g;
     stages = 2;
     A.win_cells = (int)A.res_cells;  // the padding cell follows the group's cells
-    smem = (int)smem_for(g);
+    smem = SmemLayout<Cfg>(2, (int)A.res_cells, false).total + 1024;
     grid_ll = A.n_groups < sms ? A.n_groups : sms;
   } else {
     // Window stages: in the hi/lo layout a window lives from the stencil to the epilogue (which
@@ -164,6 +173,11 @@ NCA_DECLARE_SHAPE(64, 256)
 NCA_DECLARE_SHAPE(16, 128)
 NCA_DECLARE_SHAPE(32, 256)
 #undef NCA_DECLARE_SHAPE
+
+// resident_capacity of the shapes with a resident kernel (channels below 64)
+int32_t resident_capacity_32_128(long long hw);
+int32_t resident_capacity_16_128(long long hw);
+int32_t resident_capacity_32_256(long long hw);
 
 // The attributes of one step-kernel instance (checks that the kernel image loads on a device).
 cudaError_t step_kernel_attributes(cudaFuncAttributes* fa);

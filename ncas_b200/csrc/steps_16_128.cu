@@ -26,4 +26,8 @@ int32_t launch_shape_16_128(bool split, bool noise, bool adaptive, const NcaMode
 #undef NCA_AD
 }
 
+int32_t resident_capacity_16_128(long long hw) {
+  return resident_capacity<StepCfg<16, 128, false, false, false, false, true>>(hw);
+}
+
 }  // namespace nca

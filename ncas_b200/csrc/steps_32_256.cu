@@ -26,4 +26,8 @@ int32_t launch_shape_32_256(bool split, bool noise, bool adaptive, const NcaMode
 #undef NCA_AD
 }
 
+int32_t resident_capacity_32_256(long long hw) {
+  return resident_capacity<StepCfg<32, 256, false, false, false, false, true>>(hw);
+}
+
 }  // namespace nca

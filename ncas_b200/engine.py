@@ -251,6 +251,11 @@ class B200Engine:
         return out
 
     # ------------------------------------------------------------------------- the steps
+    def resident_group(self, height: int, width: int) -> int:
+        """Whole instances of a height x width board one CTA of the resident kernel keeps in
+        shared memory (0: this model shape or board has no resident kernel)."""
+        return int(L.lib().nca_b200_resident_group(C.byref(self.desc), int(height), int(width)))
+
     def run(
         self,
         st: State,

@@ -175,3 +175,57 @@ def test_full_cfg3_pruned_rollout_sampled_boards_match_oracle():
         assert np.array_equal(res.pred[r].reshape(bc.k, -1), ref["decoded"].reshape(bc.k, -1)), r
         np.testing.assert_allclose(res.conf[r], ref["conf"], rtol=0, atol=1e-5)
         assert np.array_equal(res.cell_updates[r], ref["updates"].astype(np.float64)), r
+
+
+def _offset_model(out_offset, precision):
+    import dataclasses
+
+    from ncas_b200.model import NCA
+
+    cfg = dataclasses.replace(model_config("sudoku"), out_offset=out_offset)
+    params = synthetic_params(cfg, 0)
+    m = NCA(cfg, precision=precision)
+    with torch.no_grad():
+        for name, v in params.items():
+            m.get_parameter(name).copy_(torch.from_numpy(v))
+    return m.to(DEV).engine(), O.params_from_arrays(params, cfg)
+
+
+def _adaptive_run(eng, boards, K, depth, chunk):
+    b = eng.batch_from_boards(boards.inputs, boards.given, K)
+    n = len(boards.inputs) * K
+    st = eng.new_state(n, 81)
+    eng.init_state(st, b)
+    upd = torch.zeros(n, dtype=torch.int32, device=DEV)
+    for s0 in range(0, depth, chunk):
+        eng.run(st, b, min(chunk, depth - s0), mode="adaptive", seed=3, step0=s0, updates=upd)
+    x = eng.store_nchw(st).reshape(n, 64, 9, 9).cpu().numpy()
+    eng.check()
+    return x, upd.cpu().numpy()
+
+
+# The confidence warps read the readout slice back from the stored state: a slice across the two
+# epilogue channel halves (channels 28..36 of 64) and one ending at the last channel (55..63).
+@pytest.mark.parametrize("out_offset", [28, 55])
+def test_adaptive_readout_slice_anywhere_in_the_state_matches_oracle(out_offset):
+    eng, p = _offset_model(out_offset, "split")
+    boards = boards_for(CONFIGS["cfg4"], seed=1, n=3)
+    K, depth = 4, 12
+    x, upd = _adaptive_run(eng, boards, K, depth, depth)
+    ref = O.rollout(p, boards.inputs, boards.given, K, depth, channels=64, fire="adaptive_philox",
+                    seed=3, p_fire=0.5)
+    assert np.abs(x - ref["x"]).max() <= TOL["split"] * np.abs(ref["x"]).max()
+    assert np.array_equal(upd, ref["updates"])
+
+
+@pytest.mark.parametrize("out_offset", [1, 28, 55])
+def test_adaptive_in_kernel_confidence_equals_launch_start_confidence(out_offset):
+    # bf16 (hi/lo layout): one launch of 12 steps (the confidence warps give each next step's fire
+    # probabilities) against 12 launches of one step (each starts from the probabilities the
+    # launch-start kernel computes from the stored state): bit-identical states and counts.
+    eng, _ = _offset_model(out_offset, "bf16")
+    boards = boards_for(CONFIGS["cfg4"], seed=2, n=3)
+    x1, u1 = _adaptive_run(eng, boards, 4, 12, 12)
+    x2, u2 = _adaptive_run(eng, boards, 4, 12, 1)
+    assert np.array_equal(u1, u2)
+    assert np.array_equal(x1, x2)

@@ -83,6 +83,24 @@ def test_state_bytes(lib):
     assert lib.nca_b200_state_bytes(0, 81, 64, 0, C.byref(n)) == 1
 
 
+def test_resident_group_sizes(lib):
+    def group(C_, Hd, h, w):
+        m = L.NcaModelDesc()
+        m.channels, m.hidden = C_, Hd
+        return lib.nca_b200_resident_group(C.byref(m), h, w)
+
+    # 32 channels: a 30 x 30 maze (900 cells) fits once or more, a 201 x 201 maze does not;
+    # 64 channels have no resident kernel
+    g30 = group(32, 128, 30, 30)
+    assert g30 >= 1
+    assert group(32, 128, 201, 201) == 0
+    assert group(64, 256, 9, 9) == 0
+    # smaller boards pack more instances; 16 channels pack more than 32
+    assert group(32, 128, 9, 9) > g30
+    assert group(16, 128, 30, 30) >= g30
+    assert group(32, 128, 0, 5) == 0
+
+
 def test_invalid_arguments_are_rejected_without_a_gpu(lib):
     st = L.NcaState()
     assert lib.nca_b200_state_bind(C.byref(st), None, 0, 4, 81, 64, 0) == 1

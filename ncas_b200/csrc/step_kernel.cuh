@@ -16,6 +16,13 @@
 //   epilogue warps E1: h = relu(acc1 + b1) -> bf16 back into TMEM (A operand of GEMM2);
 //                  E2: dx = acc2 + b2, fire mask (+ noise), x' = x + f*dx, clamp, store
 //                  (src/nca/model.py:527-559, 430-438)
+//   confidence     (confidence fire rules only) after the epilogue has stored a tile, read its
+//   warps          readout slices back, evaluate the head and store each cell's fire
+//                  probability of the next step (src/nca/model.py:566-593, 596-633)
+//
+// Resident form (StepCfg::RESIDENT): each CTA keeps groups of whole instances in shared memory
+// for all steps of the launch (bf16 hi parts in two alternating buffers, the stencil's source,
+// and lo parts), reading the state from HBM when a group starts and writing it at its last step.
 //
 // Tensor memory (512 columns x 128 lanes): NZ slots holding z and one accumulator region
 // holding acc1, then h (bf16, over the columns already read) and acc2.  Every wait is bounded; a
@@ -28,9 +35,10 @@
 namespace nca {
 
 constexpr int kTileM = 128;
-// Warp roles: warp group 0 holds the MMA warp (0), the loader warp (1) and two idle warps; warp
-// groups 1-2 the 8 stencil warps (4..11); warp groups 3.. the epilogue warps (12..).  With 28
-// warps a sub-partition hosts 7 of them, so every thread has 72 registers.
+// Warp roles: warp group 0 holds the MMA warp (0), the loader warp (1) and the two confidence
+// warps (2, 3; idle without the confidence rules); warp groups 1-2 the 8 stencil warps (4..11);
+// warp groups 3-4 the 8 epilogue warps (12..19).  With 20 warps a sub-partition hosts 5 of them,
+// so every thread has 96 registers.
 constexpr int kStencilWarp0 = 4;
 constexpr int kEpiWarp0 = 12;
 

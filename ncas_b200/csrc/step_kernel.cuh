@@ -995,17 +995,25 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
         unsigned g;  // global cell
         int given;   // the cell's given byte
       };
-      auto issue = [&](Row& R, long long t, int out, int rr) {
+      // the given bytes of a tile's two rows: static data, loaded a tile ahead of their use
+      auto load_given = [&](long long t, int (&gv)[2]) {
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          const unsigned g = (unsigned)(t * kTileM) + (unsigned)(cw * 64 + rr * 32 + lane);
+          gv[rr] = 0;
+          if (t < A.n_tiles && (long long)g < total) {
+            const int inst = (int)fdiv(g, A.div_hw);
+            const int p = (int)(g - (unsigned)inst * A.HW);
+            const int row = A.inst_row ? A.inst_row[inst] : (int)fdiv((unsigned)inst, A.div_k);
+            gv[rr] = A.given[(long long)row * A.HW + p];
+          }
+        }
+      };
+      auto issue = [&](Row& R, long long t, int out, int rr, int given) {
         const int r = cw * 64 + rr * 32 + lane;
         slice_issue<Cfg, MAXC>(A, out, t, r, R.raw);
         R.g = (unsigned)(t * kTileM) + (unsigned)r;
-        R.given = 0;
-        if ((long long)R.g < total) {
-          const int inst = (int)fdiv(R.g, A.div_hw);
-          const int p = (int)(R.g - (unsigned)inst * A.HW);
-          const int row = A.inst_row ? A.inst_row[inst] : (int)fdiv((unsigned)inst, A.div_k);
-          R.given = A.given[(long long)row * A.HW + p];
-        }
+        R.given = given;
       };
       auto store = [&](const Row& R, float conf) {
         if ((long long)R.g < total)
@@ -1025,12 +1033,16 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
         store(R, conf[0]);
       };
       Row ra, rb;
+      int gnext[2];
       for (int s = 0; ok && s < A.n_steps; ++s) {
         const int out = (A.cur + s + 1) & 1;
+        load_given(blockIdx.x, gnext);
         for (long long t = blockIdx.x; t < A.n_tiles; t += grid, ++it) {
+          const int g0 = gnext[0], g1 = gnext[1];
+          load_given(t + grid, gnext);
           if (!wait_progress(s_prog, Cfg::EPI_WARPS, it + 1u, fs, W_CONF)) { ok = false; break; }
-          issue(ra, t, out, 0);
-          issue(rb, t, out, 1);
+          issue(ra, t, out, 0, g0);
+          issue(rb, t, out, 1, g1);
           if constexpr (MAXC == 9) {
             finish1(ra);
             finish1(rb);

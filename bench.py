@@ -94,7 +94,9 @@ class ClockSampler:
     def summary(self) -> dict | None:
         rows = [r.split(", ") for r in self.lines if r and r[0].isdigit()]
         if not rows:
-            return None
+            # a timed region shorter than nvidia-smi's start-up and 200 ms period (cfg0)
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "note": "timed region shorter than the 200 ms sampling period"}
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]

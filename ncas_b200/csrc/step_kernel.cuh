@@ -113,7 +113,7 @@ struct StepCfg {
   static_assert(NCH % 2 == 0, "stencil channel halves");
   static_assert(!H_IN_ACC || C <= HD / 4, "acc2 must fit next to h in the accumulator region");
   static_assert(NUM_WARPS % 4 == 0 && CH % 8 == 0, "warp groups and E2 channel shares");
-  static_assert(EPI_WARPS <= 8, "progress words of the resident mode");
+  static_assert(EPI_WARPS <= 8, "progress words (resident form, confidence warps)");
   static_assert(!RESIDENT || (!SPLIT && !HILO && !NOISE && !ADAPTIVE && !TILEDEP),
                 "the resident mode is a bf16-mode kernel without noise or confidence rules");
 };

@@ -1161,6 +1161,18 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
           s_flags[(it & 3) * kTileM + m] = (uint8_t)fl;
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars[BAR_FLAGS + (it & 3)]);
+          if (!Cfg::RESIDENT && !Cfg::TILEDEP && A.updates != nullptr) {
+            // Fired cells per instance.  With the grid barrier these warps have slack (they wait
+            // for windows) while the epilogue is on the tile's critical path, so they count;
+            // the resident form and per-tile step counters count in the epilogue instead
+            // (measured either way).
+            const unsigned grp = __match_any_sync(0xffffffffu, valid ? inst : -1);
+            const unsigned fm = __ballot_sync(0xffffffffu, (fl & 1u) != 0);
+            if (valid && lane == __ffs(grp) - 1) {
+              const int cnt = __popc(fm & grp);
+              if (cnt) atomicAdd(&A.updates[inst], (unsigned)cnt);
+            }
+          }
         }
         const bool up = valid && i > 0, dn = valid && i < A.H - 1;
         const bool lf = valid && j > 0, rt = valid && j < W - 1;
@@ -1625,7 +1637,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1) nca_step_kernel(const __grid_
             }
           }
         }
-        if (part == 0 && A.updates != nullptr) {
+        if ((Cfg::RESIDENT || Cfg::TILEDEP) && part == 0 && A.updates != nullptr) {
+          // fired cells per instance (the grid-barrier streaming form counts in the stencil)
           const bool fired = valid && f > 0.f;
           const unsigned grp = __match_any_sync(0xffffffffu, valid ? inst : -1);
           const unsigned fm = __ballot_sync(0xffffffffu, fired);
